@@ -1,0 +1,75 @@
+/*
+ * b200q -- C ABI of the B200 (sm_100a) quantised dequant-GEMM library.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t passed
+ * as void*, launches asynchronously on that stream, never allocates or frees
+ * device memory, never synchronises, and returns B200Q_OK (0) or a negative
+ * status.  b200q_last_error() gives the message of the last failure on the
+ * calling host thread.  Scratch memory ("workspace") is always caller-owned:
+ * query its size, allocate it once, zero it once; the kernels leave it in the
+ * zeroed state again when they finish (a split-K counter that the last CTA of
+ * each output strip resets).  One workspace must not be used by two launches
+ * that can overlap on the GPU.
+ *
+ * Matrix layouts are the reference's (lilian-muyaoli/kernelbench-harbor),
+ * row-major and contiguous:
+ *   x        [M, K]      activations, fp16 or bf16 (dtype argument)
+ *   qweight  [K, N/8]    int32, 8 unsigned 4-bit codes per word packed along N:
+ *                        nibble i (bits 4i..4i+3) of word [k, j] is column 8j+i
+ *   scales   [K/group, N] activation dtype
+ *   zeros    [K/group, N] activation dtype, integer-valued
+ *   y        [M, N]      activation dtype
+ *   w[k, n] = (nibble(k, n) - zeros[k/group, n]) * scales[k/group, n]
+ */
+#ifndef B200Q_H_
+#define B200Q_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200Q_OK 0
+#define B200Q_ERR_SHAPE (-1)       /* a size is out of the supported range        */
+#define B200Q_ERR_ALIGN (-2)       /* pointer or row pitch violates TMA alignment */
+#define B200Q_ERR_UNSUPPORTED (-3) /* dtype / group / mode not implemented        */
+#define B200Q_ERR_CUDA (-4)        /* a CUDA runtime call or launch failed        */
+#define B200Q_ERR_WORKSPACE (-5)   /* workspace missing or too small              */
+#define B200Q_ERR_DEVICE (-6)      /* a kernel reported a device-side error       */
+
+#define B200Q_DTYPE_FP16 0
+#define B200Q_DTYPE_BF16 1
+
+/* Library version, (major << 16) | minor. */
+int b200q_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* b200q_last_error(void);
+
+/* Reads and clears the device status word at the start of a workspace: waits
+ * for `stream`, returns 0 when no kernel reported an error, otherwise the
+ * or-ed device error bits (1 = a bounded wait timed out). Returns a negative
+ * status if the copy itself fails. */
+int b200q_workspace_status(void* workspace, void* stream);
+
+/* Bytes of zero-initialised workspace b200q_w4a16_gemm needs for this shape on
+ * `device` (the split-K decomposition depends on the SM count). */
+size_t b200q_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group, int device);
+
+/* y = x . dequant(qweight, scales, zeros).
+ * Replaces the reference operator Model.forward(x, qweight, scales, zeros) of
+ * QUANT_REF (generate_tasks.py:54-61) and its Triton oracle ModelNew.forward
+ * (common/oracles/quant_w4a16_pa.py:69-98), with y in x's dtype.
+ * Requirements: M >= 0; N % 32 == 0; K % group == 0; group in {32, 64, 128,
+ * 256}; 16-byte aligned pointers.  M == 0 is a no-op. */
+int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                     void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q_H_ */

@@ -1,0 +1,44 @@
+// extern "C" entry points: argument validation and dispatch to the kernels.
+#include "common.cuh"
+
+namespace b200q {
+size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
+int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
+                 int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
+                 size_t workspace_bytes, cudaStream_t stream);
+
+static int check_w4a16_shape(int64_t M, int64_t N, int64_t K, int64_t group, int dtype) {
+  if (dtype != B200Q_DTYPE_FP16 && dtype != B200Q_DTYPE_BF16)
+    return fail(B200Q_ERR_UNSUPPORTED, "w4a16: dtype must be fp16 (0) or bf16 (1)");
+  if (group != 32 && group != 64 && group != 128 && group != 256)
+    return fail(B200Q_ERR_UNSUPPORTED, "w4a16: group must be 32, 64, 128 or 256, got " + std::to_string(group));
+  if (M < 0 || N <= 0 || K <= 0) return fail(B200Q_ERR_SHAPE, "w4a16: M must be >= 0 and N, K > 0");
+  if (K % group) return fail(B200Q_ERR_SHAPE, "w4a16: K must be a multiple of the group size");
+  if (N % 32)
+    return fail(B200Q_ERR_ALIGN, "w4a16: N must be a multiple of 32 (qweight rows must be 16-byte pitched)");
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return fail(B200Q_ERR_SHAPE, "w4a16: size too large");
+  return B200Q_OK;
+}
+}  // namespace b200q
+
+extern "C" {
+
+size_t b200q_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group, int device) {
+  (void)group;
+  if (M <= 0 || N <= 0 || K <= 0) return 256;
+  return b200q::w4a16_decode_ws_bytes(M, N, K, device);
+}
+
+int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
+                     int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  using namespace b200q;
+  int rc = check_w4a16_shape(M, N, K, group, dtype);
+  if (rc) return rc;
+  if (M == 0) return B200Q_OK;
+  if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16: null pointer argument");
+  return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,107 @@
+"""torch custom ops over the C ABI (include/b200q.h).
+
+Each op validates its tensors the way the reference operator would see them
+(shapes of QUANT_REF.forward, generate_tasks.py:54-61), makes them contiguous
+(as the reference Triton oracle does, common/oracles/quant_w4a16_pa.py:74-77),
+allocates the output (callee-allocated, like the oracle's torch.empty at :79)
+and calls the library on the current CUDA stream.  No CPU path exists: a CPU
+tensor is an error."""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+_ws_lock = threading.Lock()
+_ws: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch owned by this process, one per (device, stream).
+    Kernels return it to the zero state, so it is allocated (and zeroed) once
+    and reused; it is never shared by two streams, whose launches could overlap."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+def reset_workspaces() -> None:
+    with _ws_lock:
+        _ws.clear()
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float16:
+        return _lib.DTYPE_FP16
+    if dt == torch.bfloat16:
+        return _lib.DTYPE_BF16
+    raise TypeError(f"activations must be float16 or bfloat16, got {dt}")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@torch.library.custom_op("b200q::w4a16_gemm", mutates_args=())
+def w4a16_gemm(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+               group: int) -> torch.Tensor:
+    """y[M, N] = x[M, K] . ((unpack(qweight) - zeros) * scales), y in x.dtype."""
+    if not x.is_cuda:
+        raise RuntimeError("b200q::w4a16_gemm runs on CUDA tensors only (no CPU implementation)")
+    if x.dim() != 2 or qweight.dim() != 2:
+        raise ValueError("x must be [M, K] and qweight [K, N/8]")
+    if qweight.dtype != torch.int32:
+        raise TypeError("qweight must be int32")
+    M, K = x.shape
+    if qweight.shape[0] != K:
+        raise ValueError(f"qweight has {qweight.shape[0]} rows, x has K={K}")
+    N = qweight.shape[1] * 8
+    if group <= 0 or K % group:
+        raise ValueError(f"K={K} is not a multiple of group={group}")
+    for name, t in (("scales", scales), ("zeros", zeros)):
+        if tuple(t.shape) != (K // group, N):
+            raise ValueError(f"{name} must be [{K // group}, {N}], got {tuple(t.shape)}")
+    dt = _dtype_code(x.dtype)
+    scales = scales.to(x.dtype)
+    zeros = zeros.to(x.dtype)
+    x, qweight, scales, zeros = (_aligned(t) for t in (x, qweight, scales, zeros))
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if M == 0:
+        return y
+    L = _lib.lib()
+    nbytes = L.b200q_w4a16_workspace_bytes(M, N, K, group, x.device.index)
+    ws = workspace(x.device, nbytes)
+    _lib.check(L.b200q_w4a16_gemm(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                                  y.data_ptr(), M, N, K, group, dt, ws.data_ptr(), ws.numel(),
+                                  _stream_ptr(x.device)))
+    return y
+
+
+@w4a16_gemm.register_fake
+def _(x, qweight, scales, zeros, group):
+    return x.new_empty((x.shape[0], qweight.shape[1] * 8))
+
+
+def device_status(device: torch.device | None = None) -> int:
+    """Reads and clears the device error word of this stream's workspace
+    (synchronises the stream).  0 means no kernel reported an error."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    ws = workspace(device, 4096)
+    r = _lib.lib().b200q_workspace_status(ws.data_ptr(), _stream_ptr(device))
+    if r < 0:
+        _lib.check(r)
+    return r

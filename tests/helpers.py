@@ -1,0 +1,71 @@
+"""Shared test helpers: seeded input builders (the reference recipe of
+QUANT_REF.get_inputs, generate_tasks.py:63-73, on a seeded generator) and a
+torch fp32 reference of the same op for sizes the numpy oracle is too slow for."""
+from __future__ import annotations
+
+import glob
+import json
+import os
+
+import numpy as np
+import torch
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = dict(rtol=1e-2, atol=1e-2)  # the benchmark's stated allclose tolerance for fp16 outputs
+
+
+def golden_cases(prefix: str):
+    return sorted(glob.glob(os.path.join(GOLDEN, prefix + "*.npz")))
+
+
+def load_case(path: str):
+    d = dict(np.load(path))
+    meta = json.loads(str(d.pop("meta"))) if "meta" in d else {}
+    return d, meta
+
+
+def np_to_torch(a: np.ndarray, dtype: str | None = None) -> torch.Tensor:
+    if dtype == "bf16":
+        return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+    return torch.from_numpy(np.ascontiguousarray(a).copy())
+
+
+def tdt(dtype: str) -> torch.dtype:
+    return {"fp16": torch.float16, "bf16": torch.bfloat16}[dtype]
+
+
+def w4a16_inputs(M, K, N, group=128, dtype="fp16", seed=0, device="cpu", dist="bj"):
+    g = torch.Generator().manual_seed(seed)
+    nib = torch.randint(0, 16, (K, N), generator=g, dtype=torch.int64)
+    packed = torch.zeros(K, N // 8, dtype=torch.int64)
+    for i in range(8):
+        packed |= nib[:, i::8] << (4 * i)
+    qweight = packed.to(torch.int32)
+    x = torch.randn(M, K, generator=g).to(tdt(dtype))
+    if dist == "bj":
+        scales = (torch.rand(K // group, N, generator=g) * 0.018 + 0.002).to(tdt(dtype))
+    else:
+        scales = (torch.randn(K // group, N, generator=g) * 0.01).to(tdt(dtype))
+    zeros = torch.randint(0, 16, (K // group, N), generator=g).to(tdt(dtype))
+    return [t.to(device) for t in (x, qweight, scales, zeros)]
+
+
+def torch_ref_fp32(x, qweight, scales, zeros, group):
+    """fp32 ground truth in torch, any device: unpack by arithmetic shift and
+    mask (generate_tasks.py:55-57), (w - z) * s in fp32, fp32 matmul."""
+    K = qweight.shape[0]
+    N = qweight.shape[1] * 8
+    shifts = torch.arange(0, 32, 4, device=qweight.device, dtype=torch.int32)
+    w = ((qweight.unsqueeze(-1) >> shifts) & 0xF).reshape(K, N).float()
+    g = K // group
+    s = scales.float().reshape(g, 1, N).expand(g, group, N).reshape(K, N)
+    z = zeros.float().reshape(g, 1, N).expand(g, group, N).reshape(K, N)
+    wd = (w - z) * s
+    if x.is_cuda:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            return x.float() @ wd
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+    return x.float() @ wd

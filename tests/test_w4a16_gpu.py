@@ -1,0 +1,107 @@
+"""W4A16 dequant-GEMM on the GPU through the C ABI, against the oracle.
+
+Tolerance: allclose(rtol=1e-2, atol=1e-2) against the fp32 ground truth (the
+benchmark's stated bar), plus a tighter check against the oracle's
+reference-module output (same fp16 dequantised weight, fp32 accumulation)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4a16 as o
+from tests.helpers import TOL, golden_cases, load_case, np_to_torch, torch_ref_fp32, w4a16_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import kernelbench_harbor_b200 as pkg
+    pkg.build()
+    from kernelbench_harbor_b200 import ops as _ops
+    return _ops
+
+
+def _run(ops, x, q, s, z, group):
+    y = ops.w4a16_gemm(x, q, s, z, group)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    return y
+
+
+@pytest.mark.parametrize("path", golden_cases("w4a16_"), ids=lambda p: p.split("/")[-1][:-4])
+def test_golden(ops, path):
+    d, m = load_case(path)
+    if m["N"] % 32:
+        pytest.skip("N not a multiple of 32")
+    dt = m["dtype"]
+    x, q, s, z = (np_to_torch(d[k], dt if k in ("x", "scales", "zeros") else None).cuda()
+                  for k in ("x", "qweight", "scales", "zeros"))
+    y = _run(ops, x, q, s, z, m["group"]).float().cpu().numpy()
+    assert y.shape == (m["M"], m["N"])
+    np.testing.assert_allclose(y, d["y_fp32"], **TOL)
+    ym = o.to_f32(d["y_module"], dt)
+    # same dequantised weight and fp32 accumulation: within a couple of output ulps
+    assert np.abs(y - ym).max() <= 4 * np.spacing(np.float16(np.abs(ym).max())) + 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 31, 32, 33, 64, 100])
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_ragged_m(ops, M, dtype):
+    x, q, s, z = w4a16_inputs(M, 1024, 512, 128, dtype, seed=M, device="cuda")
+    y = _run(ops, x, q, s, z, 128)
+    assert y.dtype == x.dtype
+    ref = o.forward_fp32(x.float().cpu().numpy(), q.cpu().numpy(), s.float().cpu().numpy(),
+                         z.float().cpu().numpy(), 128)
+    tol = TOL if dtype == "fp16" else dict(rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(y.float().cpu().numpy(), ref, **tol)
+
+
+@pytest.mark.parametrize("group", [32, 64, 128, 256])
+def test_groups(ops, group):
+    x, q, s, z = w4a16_inputs(16, 2048, 768, group, "fp16", seed=group, device="cuda")
+    y = _run(ops, x, q, s, z, group)
+    ref = torch_ref_fp32(x, q, s, z, group)
+    torch.testing.assert_close(y.float(), ref, **TOL)
+
+
+@pytest.mark.parametrize("K,N", [(128, 32), (384, 96), (4096, 14336), (14336, 4096), (3584, 18944),
+                                 (29568, 8192)])
+def test_reference_layer_shapes(ops, K, N):
+    x, q, s, z = w4a16_inputs(16, K, N, 128, "fp16", seed=K + N, device="cuda")
+    y = _run(ops, x, q, s, z, 128)
+    torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 128), **TOL)
+
+
+def test_benchmark_decode_config_vs_oracle(ops):
+    """M=16, K=14336, N=4096, g128, against the numpy oracle."""
+    x, q, s, z = w4a16_inputs(16, 14336, 4096, 128, "fp16", seed=1016, device="cuda")
+    y = _run(ops, x, q, s, z, 128).float().cpu().numpy()
+    ref = o.forward_fp32(x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy(), z.cpu().numpy(), 128)
+    np.testing.assert_allclose(y, ref, **TOL)
+
+
+def test_reference_scale_distribution(ops):
+    """The reference's own get_inputs draws scales as randn*0.01 (signed)."""
+    x, q, s, z = w4a16_inputs(16, 14336, 4096, 128, "fp16", seed=5, device="cuda", dist="ref")
+    y = _run(ops, x, q, s, z, 128)
+    torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 128), **TOL)
+
+
+def test_deterministic_and_workspace_reusable(ops):
+    x, q, s, z = w4a16_inputs(16, 14336, 4096, 128, "fp16", seed=9, device="cuda")
+    a = _run(ops, x, q, s, z, 128)
+    b = _run(ops, x, q, s, z, 128)
+    assert torch.equal(a, b)
+
+
+def test_empty_m(ops):
+    x, q, s, z = w4a16_inputs(0, 256, 64, 128, "fp16", device="cuda")
+    y = ops.w4a16_gemm(x, q, s, z, 128)
+    assert y.shape == (0, 64)
+
+
+def test_module_dropin(ops):
+    from kernelbench_harbor_b200.modules import ModelNew
+    x, q, s, z = w4a16_inputs(16, 1024, 256, 64, "fp16", seed=3, device="cuda")
+    y = ModelNew()(x, q, s, z)
+    torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 64), **TOL)
