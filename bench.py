@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark of the W4A16 g128 dequant-GEMM (and its M sweep) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Metric: W4A16 g128 GEMM us/call and % of the HBM / tensor
+roofline at M = 16 / 128 / 4096, 1-8 GPUs.  The headline workload is the
+benchmark's compute-bound configuration, x fp16 [4096, 14336] . W [14336, 4096]
+(K=14336, N=4096, group 128, asymmetric int4, scales U[0.002, 0.02], zeros
+U{0..15}); the other M values are reported in ``sweep``.  A step is one call of
+the op.  Inputs are synthetic and seeded, with the benchmark's distributions.
+
+For N > 1 GPUs (torchrun, one rank per GPU) the weight is column-sharded and
+the output all-gathered over NCCL: total work is fixed ("strong" scaling) and
+the time is the max over ranks.
+
+Timing: W untimed warm-up calls, then exactly K calls captured in a CUDA graph
+(N = 1) or launched eagerly (N > 1), bracketed by barrier + synchronize, timed
+with CUDA events on the launching stream.  Calls rotate over enough copies of
+the weights (and activations) that the working set exceeds the 126 MB L2, so
+every call streams from HBM.  SM clocks and throttle reasons are sampled with
+NVML during the timed regions.
+
+``--impl reference`` times the reference module's op sequence (a torch-CPU
+restatement of QUANT_REF.forward, oracle/reference_port.py) on the host cores
+for the same workload; each step is a column sample of the call, scaled to a
+whole call.  Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+K_DIM, N_DIM, GROUP = 14336, 4096, 128
+HEADLINE_M = 4096
+SWEEP_M = (16, 128, 1024, 4096)
+L2_BYTES = 126 * 2**20
+METRIC = "W4A16 g128 GEMM us/call & % HBM/tensor roofline at M=16/128/4096, 1-8 GPU"
+
+
+def algorithmic_bytes(M, N, K, group):
+    return K * N // 2 + 2 * (K // group) * N * 2 + M * K * 2 + M * N * 2
+
+
+def flops(M, N, K):
+    return 2 * M * N * K
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "tflops": float(d["bf16_tflops"]),
+                "tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) every ~5 ms while `active`."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.active = False
+        self.max_mhz = None
+        self._stop = False
+        self.nv = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nv = pynvml
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception as e:  # NVML unavailable: report nothing rather than guess
+            self.nv = None
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop:
+            if self.active:
+                try:
+                    mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.samples.append(mhz)
+                    for bit, name in self.REASONS.items():
+                        if r & bit:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+            time.sleep(0.005)
+
+    def summary(self):
+        self._stop = True
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------- inputs
+def make_weights(seed: int, device, K=K_DIM, N=N_DIM, group=GROUP):
+    g = torch.Generator(device=device).manual_seed(seed)
+    nib = torch.randint(0, 16, (K, N), generator=g, device=device, dtype=torch.int32)
+    packed = torch.zeros(K, N // 8, dtype=torch.int32, device=device)
+    for i in range(8):
+        packed |= nib[:, i::8] << (4 * i)
+    scales = (torch.rand(K // group, N, generator=g, device=device) * 0.018 + 0.002).half()
+    zeros = torch.randint(0, 16, (K // group, N), generator=g, device=device).half()
+    return packed, scales, zeros
+
+
+def make_x(M: int, seed: int, device, K=K_DIM):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(M, K, generator=g, device=device).half()
+
+
+# ---------------------------------------------------------------------------- our arm
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_calls(fn, n_sets, steps, warmup, world, sampler, use_graph):
+    """Per-call device time (ms) of `steps` calls rotating over `n_sets` input
+    sets, max over ranks."""
+    for i in range(max(warmup, 1)):
+        fn(i % n_sets)
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if use_graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                fn(i % n_sets)
+        g.replay()  # untimed: the first replay uploads the graph
+        barrier(world)
+        sampler.active = True
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        sampler.active = False
+    else:
+        barrier(world)
+        sampler.active = True
+        s.record()
+        for i in range(steps):
+            fn(i % n_sets)
+        e.record()
+        torch.cuda.synchronize()
+        sampler.active = False
+    barrier(world)
+    return max_over_ranks(s.elapsed_time(e) / steps, world)
+
+
+def run_ours(args, world, rank, device, peaks):
+    import kernelbench_harbor_b200 as pkg
+    pkg.build()
+    from kernelbench_harbor_b200 import ops, parallel
+    from kernelbench_harbor_b200.modules import ModelNew
+
+    sampler = ClockSampler(device.index)
+    use_graph = world == 1
+    n_local = N_DIM // world
+    w_bytes = K_DIM * n_local // 2 + 2 * (K_DIM // GROUP) * n_local * 2
+    sweep = {}
+    model = parallel.ColumnShardedW4A16(GROUP) if world > 1 else None
+    for M in sorted(set(args.sweep) | {args.m}):
+        set_bytes = w_bytes + M * K_DIM * 2
+        n_sets = max(2, min(8, -(-2 * L2_BYTES // set_bytes)))  # working set > 2x L2 where 8 sets allow
+        sets = []
+        for i in range(n_sets):
+            q, s_, z = make_weights(1000 + i, device)
+            if world > 1:
+                q, s_, z = parallel.shard_weights(q, s_, z, world, rank)
+            sets.append((make_x(M, 2000 + i, device), q, s_, z))
+        torch.cuda.synchronize()
+        if world > 1:
+            fn = lambda i: model(*sets[i])  # noqa: E731
+        else:
+            fn = lambda i: ops.w4a16_gemm(*sets[i], GROUP)  # noqa: E731
+        ms = time_calls(fn, n_sets, args.steps, args.warmup, world, sampler, use_graph)
+        us = ms * 1e3
+        ab = algorithmic_bytes(M, N_DIM, K_DIM, GROUP)
+        fl = flops(M, N_DIM, K_DIM)
+        t_hbm = ab / (peaks["hbm_gbs"] * 1e9)
+        t_ten = fl / (peaks["tflops"] * 1e12)
+        bound = "hbm" if t_hbm >= t_ten else "tensor"
+        sweep[M] = {"us_per_call": round(us, 3), "GB_s": round(ab / (us * 1e-6) / 1e9, 1),
+                    "TFLOP_s": round(fl / (us * 1e-6) / 1e12, 1), "bound": bound,
+                    "roofline_frac": round((t_hbm if bound == "hbm" else t_ten) / (us * 1e-6), 4),
+                    "l2": f"{n_sets} rotating input sets of {set_bytes / 2**20:.0f} MiB"}
+        del sets
+        torch.cuda.empty_cache()
+
+    e2e = None
+    if not args.no_e2e:
+        # the public module with HOST buffers: H2D of every forward input and
+        # D2H of y inside the timed region, each step
+        M = args.m
+        q, s_, z = make_weights(1000, device)
+        if world > 1:
+            q, s_, z = parallel.shard_weights(q, s_, z, world, rank)
+        x = make_x(M, 2000, device)
+        hx, hq, hs, hz = (t.cpu().pin_memory() for t in (x, q, s_, z))
+        hy = torch.empty((M, N_DIM), dtype=torch.float16).pin_memory()
+        mod = model if world > 1 else ModelNew()
+
+        def e2e_step():
+            dx, dq, ds, dz = (t.to(device, non_blocking=True) for t in (hx, hq, hs, hz))
+            hy.copy_(mod(dx, dq, ds, dz), non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 20))
+        for _ in range(max(args.warmup, 1)):
+            e2e_step()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(e_steps):
+            e2e_step()
+        e.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(s.elapsed_time(e) / e_steps, world)
+        e2e = {"value": round(e_ms * 1e3, 3), "unit": "us/call",
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hx, hq, hs, hz)),
+               "d2h_bytes_per_step": hy.numel() * hy.element_size(), "steps": e_steps,
+               "path": "ModelNew.forward" if world == 1 else "ColumnShardedW4A16.forward"}
+    return sweep, e2e, sampler.summary()
+
+
+# ---------------------------------------------------------------------------- CPU legs
+def cpu_reference_time(M, steps, warmup, budget_s=0.25):
+    """Median seconds of one full call of the reference op sequence on the host
+    cores, measured on a column sample (scaled by N / N_sample)."""
+    from oracle.reference_port import w4a16_forward
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    q, s_, z = make_weights(1000, torch.device("cpu"))
+    x = make_x(M, 2000, torch.device("cpu"))
+    ns = N_DIM
+    while True:  # shrink the column sample until one step fits the budget
+        t0 = time.perf_counter()
+        w4a16_forward(x, q[:, :ns // 8], s_[:, :ns], z[:, :ns], GROUP)
+        if time.perf_counter() - t0 <= budget_s or ns <= 256:
+            break
+        ns = max(256, ns // 2)
+    qs, ss, zs = q[:, :ns // 8].contiguous(), s_[:, :ns].contiguous(), z[:, :ns].contiguous()
+    for _ in range(warmup):
+        w4a16_forward(x, qs, ss, zs, GROUP)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        w4a16_forward(x, qs, ss, zs, GROUP)
+        ts.append(time.perf_counter() - t0)
+    per_call = statistics.median(ts) * (N_DIM / ns)
+    sample = (f"reference op sequence (torch CPU, fp16) on x[{M},{K_DIM}] x W[:, :{ns}] "
+              f"({ns} of {N_DIM} columns), median of {steps} steps, scaled by {N_DIM // ns}")
+    return per_call, cores, sample
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=HEADLINE_M)
+    ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=list(SWEEP_M))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    workload = f"W4A16 g{GROUP} M={args.m} K={K_DIM} N={N_DIM} fp16"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        per_call, cores, sample = cpu_reference_time(args.m, args.steps, args.warmup)
+        us = per_call * 1e6
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/call",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded, benchmark distributions)",
+            "config": {"workload": workload, "device": "host CPU"},
+            "cpu_baseline": {"value": round(us, 1), "unit": "us/call", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(us, 1), "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return 0
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", torch.cuda.current_device())
+    peaks = load_peaks()
+    sweep, e2e, clocks = run_ours(args, world, rank, device, peaks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        per_call, cores, sample = cpu_reference_time(args.m, 3, 1)
+        cpu = {"value": round(per_call * 1e6, 1), "unit": "us/call", "cores": cores, "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        M = args.m
+        head = sweep[M]
+        us = head["us_per_call"]
+        if head["bound"] == "hbm":
+            ach = algorithmic_bytes(M, N_DIM, K_DIM, GROUP) / (us * 1e-6) / 1e9
+            roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+            roof["frac"] = round(ach / peaks["hbm_gbs"], 4)
+        else:
+            ach = flops(M, N_DIM, K_DIM) / (us * 1e-6) / 1e12
+            roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peaks["tflops"], "unit": "TFLOP/s"}
+            roof["frac"] = round(ach / peaks["tflops"], 4)
+        roof["peak_source"] = ("measured (MEASURED_PEAKS.json, burst)" if peaks["source"] == "measured"
+                               else "fallback")
+        roof["traffic"] = None
+        line = {"metric": METRIC, "value": us, "unit": "us/call", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+                "data": "synthetic (seeded, benchmark distributions)",
+                "config": {"workload": workload,
+                           "parallelism": f"N-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                           "l2": head["l2"]},
+                "roofline": roof, "sweep": {str(k): v for k, v in sweep.items()},
+                "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

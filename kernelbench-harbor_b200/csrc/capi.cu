@@ -6,6 +6,13 @@ size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
 int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);
+size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
+int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y, int64_t M,
+             int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+             cudaStream_t stream);
+
+// Rows from which the tensor-core (tcgen05) path is used.
+constexpr int64_t W4A16_TC_MIN_M = 33;
 
 static int check_w4a16_shape(int64_t M, int64_t N, int64_t K, int64_t group, int dtype) {
   if (dtype != B200Q_DTYPE_FP16 && dtype != B200Q_DTYPE_BF16)
@@ -26,6 +33,7 @@ extern "C" {
 size_t b200q_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group, int device) {
   (void)group;
   if (M <= 0 || N <= 0 || K <= 0) return 256;
+  if (M >= b200q::W4A16_TC_MIN_M) return b200q::w4a16_tc_ws_bytes(M, N, K, device);
   return b200q::w4a16_decode_ws_bytes(M, N, K, device);
 }
 
@@ -37,8 +45,10 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (rc) return rc;
   if (M == 0) return B200Q_OK;
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16: null pointer argument");
-  return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes,
-                      reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (M >= W4A16_TC_MIN_M)
+    return w4a16_tc(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
+  return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
 }
 
 }  // extern "C"

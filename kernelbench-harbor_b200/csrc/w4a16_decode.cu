@@ -23,9 +23,9 @@
 //    of those words is exactly one B fragment -- no shuffles, no smem staging
 //    of dequantised values.
 //  * Split-K partials go to caller workspace slots; the last CTA of a strip
-//    (atomic ticket, no spinning) sums the slots in a fixed order, writes y
-//    and resets its ticket, so results are deterministic and the workspace is
-//    left zeroed.
+//    (atomic ticket, no spinning) sums the slots in a fixed order, writes y,
+//    clears the slots and resets its ticket, so results are deterministic and
+//    the workspace is left zeroed.
 #include "common.cuh"
 
 namespace b200q {
@@ -37,6 +37,7 @@ constexpr int KS = 128;                      // K rows per stage
 constexpr int NCONS = 8;                     // consumer warps
 constexpr int THREADS = (NCONS + 1) * 32;
 constexpr int STAGES = 6;
+constexpr int MAX_SPLITS = 16;  // split-K ranges per strip (bounded so the final sum stays in registers)
 constexpr int HEADER_BYTES = 256;  // workspace: [status int | pad] then tickets then partials
 
 template <int MT>
@@ -309,30 +310,39 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   __syncthreads();
 
+  // The CTA's output block is walked in fragment order: internal index
+  // i = ((nh * MT + mt) * 64 + e) * 32 + lane, e = tile * 4 + reg, which makes
+  // the smem reads above lane-contiguous (conflict-free).  Workspace slots use
+  // the same order; only the final store maps i to (row, column).
   const int rows_here = min(16 * MT, M - mchunk * 16 * MT);
   T* y = reinterpret_cast<T*>(y_);
-  const size_t slot_elems = (size_t)16 * MT * STRIP_COLS;
+  const int n_int = 2 * MT * 64 * 32;
+  const size_t slot_elems = (size_t)n_int;
   const size_t strip_id = (size_t)mchunk * strips + strip;
   float* my_slot = partials + (strip_id * splits + split) * slot_elems;
   const int tid = threadIdx.x;
-  for (int idx = tid; idx < rows_here * STRIP_COLS; idx += THREADS) {
-    const int row = idx / STRIP_COLS, col = idx % STRIP_COLS;
-    const int word = col >> 3, t = col & 7;
-    const int nh = word >> 4, wl = word & 15;
-    const int j = wl >> 1, om = wl & 1;
-    const int c = j >> 1, rb = j & 1;
-    const int mt = row >> 4, rr = row & 15;
-    const int g = rr & 7, r = ((rr >> 3) << 1) | rb;
-    const int ln = g * 4 + c;
-    const int e = (om * 8 + t) * 4 + r;
+  auto row_of = [](int i) {  // row within the CTA block (0 .. 16*MT-1)
+    const int ln = i & 31, e = (i >> 5) & 63;
+    const int mt = (i >> 11) % MT;
+    return mt * 16 + (ln >> 2) + ((e & 3) >> 1) * 8;
+  };
+  auto col_of = [](int i) {  // column within the 256-column strip
+    const int ln = i & 31, e = (i >> 5) & 63, nh = (i >> 11) / MT;
+    const int tile = e >> 2, r = e & 3, om = tile >> 3, t = tile & 7, c = ln & 3;
+    return 8 * (nh * 16 + 2 * (2 * c + (r & 1)) + om) + t;
+  };
+  for (int i = tid; i < n_int; i += THREADS) {
+    const int row = row_of(i);
+    if (row >= rows_here) continue;
+    const int nh = (i >> 11) / MT, rest = i - nh * MT * 2048;
     float v = 0.f;
 #pragma unroll
-    for (int kq = 0; kq < 4; ++kq) v += red[(((kq * 2 + nh) * MT + mt) * 64 + e) * 32 + ln];
-    const int gcol = strip * STRIP_COLS + col;
+    for (int kq = 0; kq < 4; ++kq) v += red[(kq * 2 + nh) * MT * 2048 + rest];
     if (splits == 1) {
+      const int gcol = strip * STRIP_COLS + col_of(i);
       if (gcol < N) y[(size_t)(mchunk * 16 * MT + row) * N + gcol] = (T)v;
     } else {
-      my_slot[idx] = v;
+      my_slot[i] = v;
     }
   }
   if (splits == 1) return;
@@ -343,13 +353,40 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const float* slots = partials + strip_id * splits * slot_elems;
-  for (int idx = tid; idx < rows_here * STRIP_COLS; idx += THREADS) {
-    float v = 0.f;
-    for (int sp = 0; sp < splits; ++sp) v += __ldcg(slots + sp * slot_elems + idx);
-    const int row = idx / STRIP_COLS, col = idx % STRIP_COLS;
-    const int gcol = strip * STRIP_COLS + col;
-    if (gcol < N) y[(size_t)(mchunk * 16 * MT + row) * N + gcol] = (T)v;
+  // all split slots of a float4 are loaded before any is summed (up to
+  // MAX_SPLITS independent L2 reads in flight per thread), then added in slot
+  // order, so the result does not depend on which CTA finished last.  The
+  // slots are cleared after reading: every workspace byte this kernel wrote
+  // goes back to zero (kernels sharing the workspace rely on zeroed memory).
+  float4* slots = reinterpret_cast<float4*>(partials + strip_id * splits * slot_elems);
+  const int slot4 = n_int / 4;
+  for (int i4 = tid; i4 < slot4; i4 += THREADS) {
+    const int i = i4 * 4;
+    const int row = row_of(i);  // the 4 lanes of a float4 share a row
+    if (row >= rows_here) continue;
+    float4 part[MAX_SPLITS];
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < splits) part[sp] = __ldcg(slots + sp * slot4 + i4);
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < splits) __stcg(slots + sp * slot4 + i4, make_float4(0.f, 0.f, 0.f, 0.f));
+    float4 v = part[0];
+#pragma unroll
+    for (int sp = 1; sp < MAX_SPLITS; ++sp)
+      if (sp < splits) {
+        v.x += part[sp].x;
+        v.y += part[sp].y;
+        v.z += part[sp].z;
+        v.w += part[sp].w;
+      }
+    T* yr = y + (size_t)(mchunk * 16 * MT + row) * N + strip * STRIP_COLS;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int col = col_of(i + q);
+      if (strip * STRIP_COLS + col < N) yr[col] = (T)vv[q];
+    }
   }
   if (tid == 0) tickets[strip_id] = 0;  // leave the workspace zeroed for the next call
 }
@@ -369,10 +406,11 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   int sp = sms / (p.strips * p.mchunks);
   if (sp < 1) sp = 1;
   if (sp > p.n_stages) sp = p.n_stages;
+  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
   p.splits = sp;
   const size_t tickets = ((size_t)p.mchunks * p.strips * 4 + 255) & ~size_t(255);
   const size_t parts =
-      p.splits > 1 ? (size_t)p.mchunks * p.strips * p.splits * 16 * p.mt * STRIP_COLS * sizeof(float) : 0;
+      p.splits > 1 ? (size_t)p.mchunks * p.strips * p.splits * (2 * p.mt * 64 * 32) * sizeof(float) : 0;
   p.ws_bytes = HEADER_BYTES + tickets + parts;
   return p;
 }

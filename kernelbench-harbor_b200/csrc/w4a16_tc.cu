@@ -1,0 +1,443 @@
+// W4A16 group-quantised GEMM on the 5th-generation tensor cores (tcgen05):
+// the compute-bound ("prefill", M >= 33) path.
+//
+// y[M, N] = x[M, K] . W[K, N],  W[k, n] = (nib(k, n) - z[k/g, n]) * s[k/g, n],
+// reference layout (QUANT_REF, generate_tasks.py:45-61): qweight [K, N/8]
+// int32 packed along N, scales / zeros [K/g, N].  The dequantised weight is
+// formed exactly as the reference rounds it ((nib - z) exact, one rounding in
+// the multiply by s, in the activation dtype) and the product accumulates in
+// fp32 in tensor memory.
+//
+// One CTA computes a 128 x 256 output tile over a K range (split-K only when
+// the tile grid cannot fill the SMs).  Warp roles:
+//   warp 0      weight producer: per 64-deep K stage, TMA of the packed weight
+//               tile [64 x 32 words] and the stage's scale / zero rows into a
+//               ring whose slots free as soon as they are dequantised;
+//   warp 2      activation producer: TMA of the x tile [128 x 64] (K-major,
+//               128B swizzle) into a ring whose slots free when the MMAs
+//               reading them complete;
+//   warp 1      owns the TMEM accumulator (256 columns) and issues, from one
+//               thread, 4 x tcgen05.mma (M128 N256 K16) per stage;
+//   warps 3..   dequantise: each converts its packed words of a stage to
+//               fp16/bf16 and stores them as the MN-major, 128B-swizzled B
+//               operand of the MMA; after the last stage they drain TMEM
+//               (tcgen05.ld) into y.
+// Nibble pairs are unpacked with one LOP3 each (magic-exponent int4 -> fp16),
+// which yields columns (0,4), (1,5), (2,6), (3,7) of a word; the B operand is
+// stored in that column order and the epilogue undoes the permutation in
+// registers.
+#include "common.cuh"
+
+namespace b200q {
+namespace tc {
+
+#ifndef B200Q_TC_SX
+#define B200Q_TC_SX 4
+#endif
+#ifndef B200Q_TC_SW
+#define B200Q_TC_SW 6
+#endif
+#ifndef B200Q_TC_S2
+#define B200Q_TC_S2 3
+#endif
+#ifndef B200Q_TC_NDQ
+#define B200Q_TC_NDQ 16
+#endif
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int SX = B200Q_TC_SX;    // x-tile ring (held until the MMAs of the stage complete)
+constexpr int SW = B200Q_TC_SW;    // packed-weight + scale/zero ring (held only until dequantised)
+constexpr int S2 = B200Q_TC_S2;    // dequantised-B ring
+constexpr int NDQ = B200Q_TC_NDQ;  // dequantising (and epilogue) warps: 8 or 16
+static_assert(NDQ == 8 || NDQ == 16, "dequant warp count");
+constexpr int WPR = NDQ / 8;    // warps per row-in-group position
+constexpr int WORDS = 8 / WPR;  // packed words per thread per stage
+constexpr int W_PROD = 0, W_MMA = 1, W_XPROD = 2, W_DQ0 = 3;  // warp roles
+constexpr int THREADS = (W_DQ0 + NDQ) * 32;
+constexpr uint32_t X_BYTES = BM * BK * 2;          // 16 KB
+constexpr uint32_t WQ_BYTES = BK * (BN / 8) * 4;   // 8 KB
+constexpr uint32_t SZ_BYTES = 2 * BN * 2;          // up to 2 scale rows per stage (group 32)
+constexpr uint32_t B_BYTES = BK * BN * 2;          // 32 KB
+constexpr uint32_t OFF_X = 0;
+constexpr uint32_t OFF_B = OFF_X + SX * X_BYTES;
+constexpr uint32_t OFF_WQ = OFF_B + S2 * B_BYTES;
+constexpr uint32_t OFF_S = OFF_WQ + SW * WQ_BYTES;
+constexpr uint32_t OFF_Z = OFF_S + SW * SZ_BYTES;
+constexpr uint32_t OFF_BAR = OFF_Z + SW * SZ_BYTES;
+constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
+constexpr int HEADER_BYTES = 256;
+constexpr int MAX_SPLITS = 16;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+static_assert((2 * SX + 2 * SW + 2 * S2 + 1) * 8 + 4 <= 256, "barrier area");
+
+template <bool BF16>
+struct DT;
+template <>
+struct DT<false> {
+  using T = __half;
+};
+template <>
+struct DT<true> {
+  using T = __nv_bfloat16;
+};
+
+__device__ __forceinline__ uint32_t as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __half2 as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+__device__ __forceinline__ __nv_bfloat162 as_b2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
+
+// Per-thread constants for the 8 columns of one packed word in one group:
+// scale pairs and zero-point terms in the (0,4)(1,5)(2,6)(3,7) pair order.
+struct ColQ {
+  uint32_t s[4], z[4];
+};
+
+template <bool BF16>
+__device__ __forceinline__ ColQ load_colq(const uint8_t* s_row, const uint8_t* z_row, int lane) {
+  const uint4 sv = *reinterpret_cast<const uint4*>(s_row + lane * 16);
+  const uint4 zv = *reinterpret_cast<const uint4*>(z_row + lane * 16);
+  ColQ q;
+  q.s[0] = prmt(sv.x, sv.z, 0x5410);
+  q.s[1] = prmt(sv.x, sv.z, 0x7632);
+  q.s[2] = prmt(sv.y, sv.w, 0x5410);
+  q.s[3] = prmt(sv.y, sv.w, 0x7632);
+  const uint32_t z04 = prmt(zv.x, zv.z, 0x5410), z15 = prmt(zv.x, zv.z, 0x7632);
+  const uint32_t z26 = prmt(zv.y, zv.w, 0x5410), z37 = prmt(zv.y, zv.w, 0x7632);
+  if (!BF16) {
+    const __half2 k1024 = __float2half2_rn(1024.f);
+    const __half2 m1 = __float2half2_rn(-1.f), m64 = __float2half2_rn(-64.f);
+    q.z[0] = as_u32(__hadd2(as_h2(z04), k1024));   // 1024 + z
+    q.z[1] = as_u32(__hfma2(as_h2(z15), m1, m64));  // -(64 + z)
+    q.z[2] = as_u32(__hadd2(as_h2(z26), k1024));
+    q.z[3] = as_u32(__hfma2(as_h2(z37), m1, m64));
+  } else {
+    const __nv_bfloat162 k128 = __float2bfloat162_rn(128.f);
+    q.z[0] = as_u32(__hadd2(as_b2(z04), k128));
+    q.z[1] = as_u32(__hadd2(as_b2(z15), k128));
+    q.z[2] = as_u32(__hadd2(as_b2(z26), k128));
+    q.z[3] = as_u32(__hadd2(as_b2(z37), k128));
+  }
+  return q;
+}
+
+// One packed word -> 8 dequantised values in pair order (n0,n4)(n1,n5)(n2,n6)(n3,n7).
+// fp16: 0x6400|n is 1024+n and 0x6400|(n<<4) is 1024+16n, so the odd positions
+// use an exact fma by 1/16; (n - z) is exact and the multiply by s is the one
+// rounding, as in the reference.  bf16: 0x4300|n is 128+n.
+template <bool BF16>
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, const ColQ& q) {
+  uint4 o;
+  if (!BF16) {
+    const __half2 r16 = __float2half2_rn(0.0625f);
+    const uint32_t w8 = w >> 8;
+    const __half2 h0 = __hsub2(as_h2(and_or(w, 0x000F000Fu, 0x64006400u)), as_h2(q.z[0]));
+    const __half2 h1 = __hfma2(as_h2(and_or(w, 0x00F000F0u, 0x64006400u)), r16, as_h2(q.z[1]));
+    const __half2 h2 = __hsub2(as_h2(and_or(w8, 0x000F000Fu, 0x64006400u)), as_h2(q.z[2]));
+    const __half2 h3 = __hfma2(as_h2(and_or(w8, 0x00F000F0u, 0x64006400u)), r16, as_h2(q.z[3]));
+    o.x = as_u32(__hmul2_rn(h0, as_h2(q.s[0])));
+    o.y = as_u32(__hmul2_rn(h1, as_h2(q.s[1])));
+    o.z = as_u32(__hmul2_rn(h2, as_h2(q.s[2])));
+    o.w = as_u32(__hmul2_rn(h3, as_h2(q.s[3])));
+  } else {
+    const __nv_bfloat162 h0 = __hsub2(as_b2(and_or(w, 0x000F000Fu, 0x43004300u)), as_b2(q.z[0]));
+    const __nv_bfloat162 h1 = __hsub2(as_b2(and_or(w >> 4, 0x000F000Fu, 0x43004300u)), as_b2(q.z[1]));
+    const __nv_bfloat162 h2 = __hsub2(as_b2(and_or(w >> 8, 0x000F000Fu, 0x43004300u)), as_b2(q.z[2]));
+    const __nv_bfloat162 h3 = __hsub2(as_b2(and_or(w >> 12, 0x000F000Fu, 0x43004300u)), as_b2(q.z[3]));
+    o.x = as_u32(__hmul2_rn(h0, as_b2(q.s[0])));
+    o.y = as_u32(__hmul2_rn(h1, as_b2(q.s[1])));
+    o.z = as_u32(__hmul2_rn(h2, as_b2(q.s[2])));
+    o.w = as_u32(__hmul2_rn(h3, as_b2(q.s[3])));
+  }
+  return o;
+}
+
+// B-operand slot -> actual column within each group of 8
+__device__ __forceinline__ int slot_col(int p) { return ((p & 1) << 2) | (p >> 1); }
+
+template <bool BF16>
+__global__ void __launch_bounds__(THREADS, 1)
+    w4a16_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wq,
+                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
+                    void* __restrict__ y_, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws) {
+  using T = typename DT<BF16>::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* x_empty = x_full + SX;
+  uint64_t* w_full = x_empty + SX;
+  uint64_t* w_empty = w_full + SW;
+  uint64_t* b_full = w_empty + SW;
+  uint64_t* b_empty = b_full + S2;
+  uint64_t* acc_full = b_empty + S2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  __shared__ int s_err, s_last;
+
+  int* status = reinterpret_cast<int*>(ws);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+  const int n0 = n_tile * BN, m0 = m_tile * BM;
+  const int nk_total = (K + BK - 1) / BK;
+  const int k_begin = (int)((long long)split * nk_total / splits);
+  const int k_end = (int)((long long)(split + 1) * nk_total / splits);
+  const int nk = k_end - k_begin;
+  const int srows = group >= BK ? 1 : BK / group;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
+    }
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], NDQ);
+    }
+    for (int j = 0; j < S2; ++j) {
+      mbar_init(&b_full[j], NDQ);
+      mbar_init(&b_empty[j], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+    s_err = 0;
+  }
+  if (warp == W_PROD && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_wq);
+    prefetch_tmap(&tm_s);
+    prefetch_tmap(&tm_z);
+  }
+  if (warp == W_MMA) tmem_alloc(tmem_slot, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == W_PROD) {
+    // ---------------------------------------------------------------- weight producer
+    if (lane == 0) {
+      const uint32_t stage_tx = WQ_BYTES + 2u * srows * BN * 2u;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % SW;
+        if (it >= SW && !mbar_wait(&w_empty[s], ((it / SW) - 1) & 1, status)) {
+          s_err = 1;
+          break;
+        }
+        const int kb = (k_begin + it) * BK;
+        mbar_arrive_expect_tx(&w_full[s], stage_tx);
+        tma_load_2d(smem + OFF_WQ + s * WQ_BYTES, &tm_wq, n0 / 8, kb, &w_full[s]);
+        tma_load_2d(smem + OFF_S + s * SZ_BYTES, &tm_s, n0, kb / group, &w_full[s]);
+        tma_load_2d(smem + OFF_Z + s * SZ_BYTES, &tm_z, n0, kb / group, &w_full[s]);
+      }
+    }
+  } else if (warp == W_XPROD) {
+    // ---------------------------------------------------------------- activation producer
+    if (lane == 0) {
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % SX;
+        if (it >= SX && !mbar_wait(&x_empty[s], ((it / SX) - 1) & 1, status)) {
+          s_err = 1;
+          break;
+        }
+        const int kb = (k_begin + it) * BK;
+        mbar_arrive_expect_tx(&x_full[s], X_BYTES);
+        tma_load_2d(smem + OFF_X + s * X_BYTES, &tm_x, kb, m0, &x_full[s]);
+      }
+    }
+  } else if (warp == W_MMA) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BM, BN, BF16 ? 1 : 0, /*a_mn=*/0, /*b_mn=*/1);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % SX, j = it % S2;
+        if (!mbar_wait(&x_full[s], (it / SX) & 1, status) || !mbar_wait(&b_full[j], (it / S2) & 1, status)) {
+          s_err = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xa = smem_u32(smem + OFF_X + s * X_BYTES);
+        const uint32_t bb = smem_u32(smem + OFF_B + j * B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // A: K-major, 8-row groups 1024 B apart; B: MN-major, 64-column atoms
+          // 1024 B apart, 8-row K groups 4096 B apart
+          const uint64_t ad = smem_desc(xa + kk * 32, 16, 1024, 2);
+          const uint64_t bd = smem_desc(bb + kk * 8192, 1024, 4096, 2);
+          tc_mma_f16_ss(tmem, ad, bd, idesc, (it | kk) != 0);
+        }
+        tc_commit(&x_empty[s]);
+        tc_commit(&b_empty[j]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ---------------------------------------------------------------- dequantise
+    const int dw = warp - W_DQ0;
+    const int nb = lane >> 3, ch = lane & 7;
+    const int rr = dw & 7;  // row within each 8-row group
+    for (int it = 0; it < nk; ++it) {
+      const int s = it % SW, j = it % S2;
+      if (!mbar_wait(&w_full[s], (it / SW) & 1, status)) {
+        s_err = 1;
+        break;
+      }
+      if (it >= S2 && !mbar_wait(&b_empty[j], ((it / S2) - 1) & 1, status)) {
+        s_err = 1;
+        break;
+      }
+      const uint32_t* wq = reinterpret_cast<const uint32_t*>(smem + OFF_WQ + s * WQ_BYTES);
+      const uint8_t* srow0 = smem + OFF_S + s * SZ_BYTES;
+      const uint8_t* zrow0 = smem + OFF_Z + s * SZ_BYTES;
+      uint8_t* bslot = smem + OFF_B + j * B_BYTES;
+      // packed words and scale/zero constants go to registers first, so the
+      // weight slot is released before the dequantised stores start
+      const ColQ q0 = load_colq<BF16>(srow0, zrow0, lane);
+      const ColQ q1 = srows > 1 ? load_colq<BF16>(srow0 + BN * 2, zrow0 + BN * 2, lane) : q0;
+      uint32_t wv[WORDS];
+#pragma unroll
+      for (int i = 0; i < WORDS; ++i) wv[i] = wq[(rr + 8 * (WPR * i + (dw >> 3))) * 32 + lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&w_empty[s]);
+#pragma unroll
+      for (int i = 0; i < WORDS; ++i) {
+        const int kg = WPR * i + (dw >> 3);  // 8-row group 0..7; group 32 switches scale row at kg 4
+        const uint4 v = dequant_word<BF16>(wv[i], (srows > 1 && kg >= 4) ? q1 : q0);
+        *reinterpret_cast<uint4*>(bslot + (kg * 4 + nb) * 1024 + rr * 128 + ((ch ^ rr) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_full[j]);
+    }
+
+    // ---------------------------------------------------------------- epilogue: TMEM -> y
+    if (!s_err && mbar_wait(acc_full, 0, status)) {
+      tc_fence_after();
+      const int qd = warp & 3;   // TMEM lane quadrant this warp may access
+      const int part = dw >> 2;  // which of the NDQ/4 column ranges of this quadrant
+      constexpr int COLS = BN / (NDQ / 4);
+      const int row = m0 + qd * 32 + lane;
+      T* y = reinterpret_cast<T*>(y_);
+      float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
+#pragma unroll 1
+      for (int c0 = 0; c0 < COLS; c0 += 32) {
+        const int cslot = part * COLS + c0;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + cslot, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int p = 0; p < 32; ++p) v[(p & ~7) | slot_col(p & 7)] = __uint_as_float(r[p]);
+        const int col = n0 + cslot;
+        if (row < M && col < N) {
+          if (splits == 1) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int p = 0; p < 16; ++p) {
+              if (!BF16)
+                packed[p] = as_u32(__floats2half2_rn(v[2 * p], v[2 * p + 1]));
+              else
+                packed[p] = as_u32(__floats2bfloat162_rn(v[2 * p], v[2 * p + 1]));
+            }
+            uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * N + col);
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+              dst[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+          } else {
+            float4* dst = reinterpret_cast<float4*>(acc_ws + (size_t)row * N + col);
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+              atomicAdd(dst + p, make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (splits > 1 && !s_err) {
+    // split-K: the last CTA of this output tile converts the fp32 sum and
+    // clears it (and the ticket), returning the workspace to zero.
+    __threadfence();
+    __syncthreads();
+    int* tickets = reinterpret_cast<int*>(ws + HEADER_BYTES + (size_t)M * N * 4);
+    const int tile_id = m_tile * gridDim.x + n_tile;
+    if (threadIdx.x == 0) s_last = atomicAdd(&tickets[tile_id], 1) == splits - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
+      T* y = reinterpret_cast<T*>(y_);
+      const int rows = min(BM, M - m0), cols = min(BN, N - n0);
+      for (int e = threadIdx.x * 4; e < rows * cols; e += THREADS * 4) {
+        const int rr = e / cols, cc = e % cols;  // cols % 32 == 0: a float4 never straddles rows
+        float4* src = reinterpret_cast<float4*>(acc_ws + (size_t)(m0 + rr) * N + n0 + cc);
+        const float4 a = __ldcg(src);
+        T* d = y + (size_t)(m0 + rr) * N + n0 + cc;
+        d[0] = (T)a.x;
+        d[1] = (T)a.y;
+        d[2] = (T)a.z;
+        d[3] = (T)a.w;
+        __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+      if (threadIdx.x == 0) tickets[tile_id] = 0;
+    }
+  }
+  if (warp == W_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+struct Plan {
+  int tiles_m, tiles_n, splits;
+  size_t ws_bytes;
+};
+
+Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
+  Plan p;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  const int nk = (int)((K + BK - 1) / BK);
+  int sp = sms / (p.tiles_m * p.tiles_n);
+  if (sp < 1) sp = 1;
+  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
+  if (sp > nk / 4) sp = nk / 4 > 0 ? nk / 4 : 1;  // keep >= 4 stages per split
+  p.splits = sp;
+  p.ws_bytes = HEADER_BYTES + (sp > 1 ? (size_t)M * N * 4 + (size_t)p.tiles_m * p.tiles_n * 4 : 0);
+  return p;
+}
+
+}  // namespace tc
+
+size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
+  return tc::plan(M, N, K, num_sms(device)).ws_bytes;
+}
+
+int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y, int64_t M,
+             int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+             cudaStream_t stream) {
+  using namespace tc;
+  const Plan p = plan(M, N, K, num_sms(-1));
+  if (!workspace || workspace_bytes < p.ws_bytes)
+    return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(p.ws_bytes) + " bytes required");
+  const CUtensorMapDataType h16 = CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const uint32_t srows = group >= BK ? 1 : (uint32_t)(BK / group);
+  CUtensorMap tx, twq, ts, tz;
+  int rc;
+  if ((rc = encode_2d(&tx, h16, x, K, M, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = encode_2d(&twq, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N / 8, K, (uint64_t)N / 2, BN / 8, BK,
+                      CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = encode_2d(&ts, h16, scales, N, K / group, (uint64_t)N * 2, BN, srows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = encode_2d(&tz, h16, zeros, N, K / group, (uint64_t)N * 2, BN, srows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  auto kern = dtype == B200Q_DTYPE_BF16 ? w4a16_tc_kernel<true> : w4a16_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 tc)");
+  dim3 grid(p.tiles_n, p.tiles_m, p.splits);
+  kern<<<grid, THREADS, SMEM, stream>>>(tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
+                                        reinterpret_cast<uint8_t*>(workspace));
+  return check_cuda(cudaGetLastError(), "w4a16 tc launch");
+}
+
+}  // namespace b200q

@@ -69,3 +69,39 @@ def torch_ref_fp32(x, qweight, scales, zeros, group):
         finally:
             torch.backends.cuda.matmul.allow_tf32 = prev
     return x.float() @ wd
+
+
+def torch_ref_module(x, qweight, scales, zeros, group):
+    """The reference module's own numerics (generate_tasks.py:55-61): the
+    dequantised weight is rounded to x.dtype exactly as QUANT_REF does it
+    ((w - ze) then * se, each in x.dtype); the product accumulates in fp32 and
+    is returned in fp32 (before the module's final rounding to x.dtype)."""
+    K = qweight.shape[0]
+    N = qweight.shape[1] * 8
+    shifts = torch.arange(0, 32, 4, device=qweight.device, dtype=torch.int32)
+    w = ((qweight.unsqueeze(-1) >> shifts) & 0xF).reshape(K, N).to(x.dtype)
+    g = K // group
+    se = scales.reshape(g, 1, N).expand(g, group, N).reshape(K, N).to(x.dtype)
+    ze = zeros.reshape(g, 1, N).expand(g, group, N).reshape(K, N).to(x.dtype)
+    wd = ((w - ze) * se).float()
+    if x.is_cuda:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            return x.float() @ wd
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+    return x.float() @ wd
+
+
+def check_w4a16(y, x, qweight, scales, zeros, group):
+    """fp16: allclose(1e-2) against the fp32 ground truth.  bf16: the
+    reference module itself rounds the weight to bf16 (8 significant bits), so
+    the output is held to allclose(1e-2) against that module's numerics and to
+    allclose(5e-2) against the fp32 ground truth."""
+    ref32 = torch_ref_fp32(x, qweight, scales, zeros, group)
+    if x.dtype == torch.float16:
+        torch.testing.assert_close(y.float(), ref32, **TOL)
+    else:
+        torch.testing.assert_close(y.float(), torch_ref_module(x, qweight, scales, zeros, group), **TOL)
+        torch.testing.assert_close(y.float(), ref32, rtol=5e-2, atol=5e-2)

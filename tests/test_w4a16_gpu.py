@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import w4a16 as o
-from tests.helpers import TOL, golden_cases, load_case, np_to_torch, torch_ref_fp32, w4a16_inputs
+from tests.helpers import TOL, check_w4a16, golden_cases, load_case, np_to_torch, torch_ref_fp32, w4a16_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -50,10 +50,10 @@ def test_ragged_m(ops, M, dtype):
     x, q, s, z = w4a16_inputs(M, 1024, 512, 128, dtype, seed=M, device="cuda")
     y = _run(ops, x, q, s, z, 128)
     assert y.dtype == x.dtype
-    ref = o.forward_fp32(x.float().cpu().numpy(), q.cpu().numpy(), s.float().cpu().numpy(),
-                         z.float().cpu().numpy(), 128)
-    tol = TOL if dtype == "fp16" else dict(rtol=2e-2, atol=2e-2)
-    np.testing.assert_allclose(y.float().cpu().numpy(), ref, **tol)
+    if dtype == "fp16":
+        ref = o.forward_fp32(x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy(), z.cpu().numpy(), 128)
+        np.testing.assert_allclose(y.float().cpu().numpy(), ref, **TOL)
+    check_w4a16(y, x, q, s, z, 128)
 
 
 @pytest.mark.parametrize("group", [32, 64, 128, 256])
@@ -105,3 +105,37 @@ def test_module_dropin(ops):
     x, q, s, z = w4a16_inputs(16, 1024, 256, 64, "fp16", seed=3, device="cuda")
     y = ModelNew()(x, q, s, z)
     torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 64), **TOL)
+
+
+@pytest.mark.parametrize("M,K,N,group,dtype", [
+    (128, 14336, 4096, 128, "fp16"),   # benchmark config 1 (split-K tiles)
+    (256, 1024, 512, 128, "fp16"),
+    (300, 2048, 768, 64, "fp16"),      # ragged M tile, ragged N tile (768 = 3 x 256)
+    (129, 4096, 1024, 32, "bf16"),
+    (512, 4096, 1024, 256, "bf16"),
+    (1024, 14336, 4096, 128, "fp16"),  # benchmark config 1
+])
+def test_tensor_core_path(ops, M, K, N, group, dtype):
+    x, q, s, z = w4a16_inputs(M, K, N, group, dtype, seed=M + K, device="cuda")
+    y = _run(ops, x, q, s, z, group)
+    check_w4a16(y, x, q, s, z, group)
+
+
+def test_tensor_core_full_config(ops):
+    """BASELINE config 1 at M=4096 against the fp32 torch reference."""
+    x, q, s, z = w4a16_inputs(4096, 14336, 4096, 128, "fp16", seed=4096, device="cuda")
+    y = _run(ops, x, q, s, z, 128)
+    torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 128), **TOL)
+
+
+def test_workspace_left_zeroed(ops):
+    """Every kernel returns the workspace it used to zero, so kernels of
+    different shapes can share it (decode split-K slots, tensor-core split-K
+    accumulator and tickets)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    for M in (16, 128, 5, 200):
+        x, q, s, z = w4a16_inputs(M, 4096, 1024, 128, "fp16", seed=M, device="cuda")
+        _run(ops, x, q, s, z, 128)
+        ws = ops.workspace(dev, 0)
+        torch.cuda.synchronize()
+        assert int(ws.count_nonzero()) == 0, f"workspace dirty after M={M}"
