@@ -68,6 +68,19 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
                      void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* y = x . dequant(qweight, scales, zeros) for 1 <= M <= 32, with no workspace
+ * argument and no allocation: for callers that cannot call cudaMalloc (a
+ * plugin inside a host program that owns all device memory, a fixed memory
+ * budget).  No counterpart in the reference; it is an addition of this
+ * library.  Its split-K scratch is a fixed 8 MiB device array inside the
+ * library, held on every GPU that loads it until exit; shapes needing more are
+ * rejected with B200Q_ERR_SHAPE.  The first call on a device looks up that
+ * array's address and should come before any stream capture.  All calls share
+ * the array, so calls that can overlap on the GPU race: serialise them.  Same
+ * layouts, requirements and results as b200q_w4a16_gemm. */
+int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                             void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
