@@ -8,16 +8,18 @@
 // the multiply by s, in the activation dtype) and the product accumulates in
 // fp32 in tensor memory.
 //
-// One CTA computes a 128 x 256 output tile over a K range (split-K only when
-// the tile grid cannot fill the SMs).  Warp roles:
+// One CTA computes a 128 x 256 or 256 x 256 output tile (MB = 1 or 2 blocks
+// of 128 rows sharing every dequantised weight tile, one TMEM accumulator of
+// 256 columns each) over a K range (split-K only when the tile grid cannot
+// fill the SMs).  Warp roles:
 //   warp 0      weight producer: per 64-deep K stage, TMA of the packed weight
 //               tile [64 x 32 words] and the stage's scale / zero rows into a
 //               ring whose slots free as soon as they are dequantised;
 //   warp 2      activation producer: TMA of the x tile [128 x 64] (K-major,
 //               128B swizzle) into a ring whose slots free when the MMAs
 //               reading them complete;
-//   warp 1      owns the TMEM accumulator (256 columns) and issues, from one
-//               thread, 4 x tcgen05.mma (M128 N256 K16) per stage;
+//   warp 1      owns the TMEM accumulators and issues, from one thread,
+//               4 x MB tcgen05.mma (M128 N256 K16) per stage;
 //   warps 3..   dequantise: each converts its packed words of a stage to
 //               fp16/bf16 and stores them as the MN-major, 128B-swizzled B
 //               operand of the MMA; after the last stage they drain TMEM
@@ -31,44 +33,38 @@
 namespace b200q {
 namespace tc {
 
-#ifndef B200Q_TC_SX
-#define B200Q_TC_SX 4
-#endif
-#ifndef B200Q_TC_SW
-#define B200Q_TC_SW 6
-#endif
-#ifndef B200Q_TC_S2
-#define B200Q_TC_S2 3
-#endif
-#ifndef B200Q_TC_NDQ
-#define B200Q_TC_NDQ 16
-#endif
-
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int SX = B200Q_TC_SX;    // x-tile ring (held until the MMAs of the stage complete)
-constexpr int SW = B200Q_TC_SW;    // packed-weight + scale/zero ring (held only until dequantised)
-constexpr int S2 = B200Q_TC_S2;    // dequantised-B ring
-constexpr int NDQ = B200Q_TC_NDQ;  // dequantising (and epilogue) warps: 8 or 16
-static_assert(NDQ == 8 || NDQ == 16, "dequant warp count");
+constexpr int NDQ = 16;         // dequantising (and epilogue) warps
 constexpr int WPR = NDQ / 8;    // warps per row-in-group position
 constexpr int WORDS = 8 / WPR;  // packed words per thread per stage
 constexpr int W_PROD = 0, W_MMA = 1, W_XPROD = 2, W_DQ0 = 3;  // warp roles
 constexpr int THREADS = (W_DQ0 + NDQ) * 32;
-constexpr uint32_t X_BYTES = BM * BK * 2;          // 16 KB
+constexpr uint32_t XB_BYTES = BM * BK * 2;         // one 128-row x box: 16 KB
 constexpr uint32_t WQ_BYTES = BK * (BN / 8) * 4;   // 8 KB
 constexpr uint32_t SZ_BYTES = 2 * BN * 2;          // up to 2 scale rows per stage (group 32)
 constexpr uint32_t B_BYTES = BK * BN * 2;          // 32 KB
-constexpr uint32_t OFF_X = 0;
-constexpr uint32_t OFF_B = OFF_X + SX * X_BYTES;
-constexpr uint32_t OFF_WQ = OFF_B + S2 * B_BYTES;
-constexpr uint32_t OFF_S = OFF_WQ + SW * WQ_BYTES;
-constexpr uint32_t OFF_Z = OFF_S + SW * SZ_BYTES;
-constexpr uint32_t OFF_BAR = OFF_Z + SW * SZ_BYTES;
-constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
 constexpr int HEADER_BYTES = 256;
 constexpr int MAX_SPLITS = 16;
-static_assert(SMEM <= 227 * 1024, "shared memory budget");
-static_assert((2 * SX + 2 * SW + 2 * S2 + 1) * 8 + 4 <= 256, "barrier area");
+
+// MB = number of 128-row blocks of x per CTA sharing each dequantised B tile
+// (1: 128 x 256 tile, 256 TMEM columns; 2: 256 x 256 tile, all 512 columns).
+template <int MB>
+struct Cfg {
+  static constexpr int SX = MB == 1 ? 4 : 3;  // x ring (held until the MMAs of the stage complete)
+  static constexpr int SW = MB == 1 ? 6 : 4;  // packed-weight + scale/zero ring (held until dequantised)
+  static constexpr int S2 = MB == 1 ? 3 : 2;  // dequantised-B ring
+  static constexpr uint32_t X_BYTES = MB * XB_BYTES;
+  static constexpr uint32_t OFF_X = 0;
+  static constexpr uint32_t OFF_B = OFF_X + SX * X_BYTES;
+  static constexpr uint32_t OFF_WQ = OFF_B + S2 * B_BYTES;
+  static constexpr uint32_t OFF_S = OFF_WQ + SW * WQ_BYTES;
+  static constexpr uint32_t OFF_Z = OFF_S + SW * SZ_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_Z + SW * SZ_BYTES;
+  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = MB * BN;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert((2 * SX + 2 * SW + 2 * S2 + 1) * 8 + 4 <= 256, "barrier area");
+};
 
 template <bool BF16>
 struct DT;
@@ -154,12 +150,16 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, const ColQ& q) {
 // B-operand slot -> actual column within each group of 8
 __device__ __forceinline__ int slot_col(int p) { return ((p & 1) << 2) | (p >> 1); }
 
-template <bool BF16>
+template <bool BF16, int MB>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wq,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                     void* __restrict__ y_, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws) {
   using T = typename DT<BF16>::T;
+  using C = Cfg<MB>;
+  constexpr int SX = C::SX, SW = C::SW, S2 = C::S2;
+  constexpr uint32_t X_BYTES = C::X_BYTES, OFF_X = C::OFF_X, OFF_B = C::OFF_B, OFF_WQ = C::OFF_WQ,
+                     OFF_S = C::OFF_S, OFF_Z = C::OFF_Z, OFF_BAR = C::OFF_BAR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* x_full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   int* status = reinterpret_cast<int*>(ws);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
-  const int n0 = n_tile * BN, m0 = m_tile * BM;
+  const int n0 = n_tile * BN, m0 = m_tile * BM * MB;
   const int nk_total = (K + BK - 1) / BK;
   const int k_begin = (int)((long long)split * nk_total / splits);
   const int k_end = (int)((long long)(split + 1) * nk_total / splits);
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_s);
     prefetch_tmap(&tm_z);
   }
-  if (warp == W_MMA) tmem_alloc(tmem_slot, BN);
+  if (warp == W_MMA) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -239,7 +239,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const int kb = (k_begin + it) * BK;
         mbar_arrive_expect_tx(&x_full[s], X_BYTES);
-        tma_load_2d(smem + OFF_X + s * X_BYTES, &tm_x, kb, m0, &x_full[s]);
+#pragma unroll
+        for (int mb = 0; mb < MB; ++mb)
+          tma_load_2d(smem + OFF_X + s * X_BYTES + mb * XB_BYTES, &tm_x, kb, m0 + mb * BM, &x_full[s]);
       }
     }
   } else if (warp == W_MMA) {
@@ -259,9 +261,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kk = 0; kk < BK / 16; ++kk) {
           // A: K-major, 8-row groups 1024 B apart; B: MN-major, 64-column atoms
           // 1024 B apart, 8-row K groups 4096 B apart
-          const uint64_t ad = smem_desc(xa + kk * 32, 16, 1024, 2);
           const uint64_t bd = smem_desc(bb + kk * 8192, 1024, 4096, 2);
-          tc_mma_f16_ss(tmem, ad, bd, idesc, (it | kk) != 0);
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) {
+            const uint64_t ad = smem_desc(xa + mb * XB_BYTES + kk * 32, 16, 1024, 2);
+            tc_mma_f16_ss(tmem + mb * BN, ad, bd, idesc, (it | kk) != 0);
+          }
         }
         tc_commit(&x_empty[s]);
         tc_commit(&b_empty[j]);
@@ -312,15 +317,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int qd = warp & 3;   // TMEM lane quadrant this warp may access
       const int part = dw >> 2;  // which of the NDQ/4 column ranges of this quadrant
-      constexpr int COLS = BN / (NDQ / 4);
-      const int row = m0 + qd * 32 + lane;
+      constexpr int COLS = MB * BN / (NDQ / 4);  // lies within one accumulator
+      const int acc = (part * COLS) / BN;
+      const int row = m0 + acc * BM + qd * 32 + lane;
       T* y = reinterpret_cast<T*>(y_);
       float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
 #pragma unroll 1
       for (int c0 = 0; c0 < COLS; c0 += 32) {
-        const int cslot = part * COLS + c0;
+        const int tcol = part * COLS + c0;  // TMEM column: accumulator acc, column tcol % BN
+        const int cslot = tcol % BN;
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + cslot, r);
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + tcol, r);
         tmem_ld_wait();
         float v[32];
 #pragma unroll
@@ -366,7 +373,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __threadfence();
       float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
       T* y = reinterpret_cast<T*>(y_);
-      const int rows = min(BM, M - m0), cols = min(BN, N - n0);
+      const int rows = min(BM * MB, M - m0), cols = min(BN, N - n0);
       for (int e = threadIdx.x * 4; e < rows * cols; e += THREADS * 4) {
         const int rr = e / cols, cc = e % cols;  // cols % 32 == 0: a float4 never straddles rows
         float4* src = reinterpret_cast<float4*>(acc_ws + (size_t)(m0 + rr) * N + n0 + cc);
@@ -383,19 +390,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == W_MMA) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
 struct Plan {
-  int tiles_m, tiles_n, splits;
+  int mb, tiles_m, tiles_n, splits;
   size_t ws_bytes;
 };
 
 Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   Plan p;
-  p.tiles_m = (int)((M + BM - 1) / BM);
+  // 256-row tiles halve the dequantisation per FLOP; used when they alone
+  // give at least one CTA per SM (otherwise 128-row tiles fill the GPU better)
   p.tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * p.tiles_n;
+  p.mb = tiles2 >= sms ? 2 : 1;
+  p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
   const int nk = (int)((K + BK - 1) / BK);
   int sp = sms / (p.tiles_m * p.tiles_n);
   if (sp < 1) sp = 1;
@@ -431,11 +442,14 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
     return rc;
   if ((rc = encode_2d(&tz, h16, zeros, N, K / group, (uint64_t)N * 2, BN, srows, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  auto kern = dtype == B200Q_DTYPE_BF16 ? w4a16_tc_kernel<true> : w4a16_tc_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  const bool bf = dtype == B200Q_DTYPE_BF16;
+  auto kern = p.mb == 2 ? (bf ? w4a16_tc_kernel<true, 2> : w4a16_tc_kernel<false, 2>)
+                        : (bf ? w4a16_tc_kernel<true, 1> : w4a16_tc_kernel<false, 1>);
+  const uint32_t smem = p.mb == 2 ? Cfg<2>::SMEM : Cfg<1>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 tc)");
   dim3 grid(p.tiles_n, p.tiles_m, p.splits);
-  kern<<<grid, THREADS, SMEM, stream>>>(tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
+  kern<<<grid, THREADS, smem, stream>>>(tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
                                         reinterpret_cast<uint8_t*>(workspace));
   return check_cuda(cudaGetLastError(), "w4a16 tc launch");
 }
