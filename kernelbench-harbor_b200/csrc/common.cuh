@@ -18,6 +18,9 @@
 
 #include "b200q.h"
 
+#ifndef B200Q_WAIT_SLEEP_NS
+#define B200Q_WAIT_SLEEP_NS 100000  // suspend-time hint of mbarrier waits in ns (0: plain polling)
+#endif
 #ifndef B200Q_WAIT_NS
 #define B200Q_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait in these kernels
 #endif
@@ -111,7 +114,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+#if B200Q_WAIT_SLEEP_NS > 0
+    if (mbar_try_wait_sleep(bar, parity, B200Q_WAIT_SLEEP_NS)) return true;
+#else
+    if (mbar_try_wait(bar, parity)) return true;
+#endif
     if ((i & 63) == 0) {
       const uint64_t t = globaltimer();
       if (i == 0) {
@@ -180,6 +187,11 @@ __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t mask, uint32_t b
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bits));
   return r;
+}
+
+// Hardware named barrier `id` (1..15) over `threads` threads (a multiple of 32).
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ uint32_t elect_one_sync() {
