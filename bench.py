@@ -46,6 +46,7 @@ K_DIM, N_DIM, GROUP = 14336, 4096, 128
 HEADLINE_M = 4096
 SWEEP_M = (16, 128, 1024, 4096)
 L2_BYTES = 126 * 2**20
+NCU_TRAFFIC = {4096: 209_088_512}  # 186.118912 MB read + 22.969600 MB written
 METRIC = "W4A16 g128 GEMM us/call & % HBM/tensor roofline at M=16/128/4096, 1-8 GPU"
 
 
@@ -355,7 +356,10 @@ def main():
             roof["frac"] = round(ach / peaks["tflops"], 4)
         roof["peak_source"] = ("measured (MEASURED_PEAKS.json, burst)" if peaks["source"] == "measured"
                                else "fallback")
-        roof["traffic"] = None
+        # DRAM bytes (read + write) of one launch of the headline kernel, from
+        # the ncu capture `ncu --set full ... profile_case --m 4096` summarised
+        # in profiles/w4a16_tc_m4096.md; None for workloads not captured
+        roof["traffic"] = NCU_TRAFFIC.get(M)
         line = {"metric": METRIC, "value": us, "unit": "us/call", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
                 "scaling": "strong", "vs_baseline": None, "dtype": "fp16",

@@ -1,0 +1,41 @@
+"""One small, seeded W4A16 case for profilers (ncu): builds the benchmark's
+inputs on the GPU and calls the op a few times.
+
+    python -m kernelbench_harbor_b200.profile_case --m 4096 --calls 2
+    ncu --set full --clock-control none -k regex:w4a16 -s 1 -c 1 \\
+        python -m kernelbench_harbor_b200.profile_case --m 4096 --calls 2
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def inputs(M: int, K: int = 14336, N: int = 4096, group: int = 128, seed: int = 1, device: str = "cuda"):
+    g = torch.Generator(device=device).manual_seed(seed)
+    nib = torch.randint(0, 16, (K, N), generator=g, device=device, dtype=torch.int32)
+    q = torch.zeros(K, N // 8, dtype=torch.int32, device=device)
+    for i in range(8):
+        q |= nib[:, i::8] << (4 * i)
+    s = (torch.rand(K // group, N, generator=g, device=device) * 0.018 + 0.002).half()
+    z = torch.randint(0, 16, (K // group, N), generator=g, device=device).half()
+    x = torch.randn(M, K, generator=g, device=device).half()
+    return x, q, s, z
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--m", type=int, default=16)
+    ap.add_argument("--calls", type=int, default=2)
+    args = ap.parse_args()
+    from . import ops
+    x, q, s, z = inputs(args.m)
+    for _ in range(args.calls):
+        ops.w4a16_gemm(x, q, s, z, 128)
+    torch.cuda.synchronize()
+    print("ok")
+
+
+if __name__ == "__main__":
+    main()
