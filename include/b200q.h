@@ -68,6 +68,19 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
                      void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of zero-initialised workspace b200q_w8a8_gemm needs for this shape. */
+size_t b200q_w8a8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device);
+
+/* y[M, N] = fp16((x_int8 . w_int8) * x_scale[m] * w_scale[n]), int32 accumulation.
+ * Replaces W8A8_REF.forward(x_int8, w_int8, x_scale, w_scale)
+ * (generate_tasks.py:204-206): x_int8 [M, K] int8, w_int8 [K, N] int8 (N
+ * contiguous), x_scale [M] fp16 (the reference's [M, 1]), w_scale [N] fp16
+ * (its [1, N]), y [M, N] fp16.  Requirements: K % 16 == 0, N % 32 == 0,
+ * 16-byte aligned pointers.  The product is exact (int32); the reference's
+ * fp32 matmul rounds it. */
+int b200q_w8a8_gemm(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y,
+                    int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* y = x . dequant(qweight, scales, zeros) for 1 <= M <= 32, with no workspace
  * argument and no allocation: for callers that cannot call cudaMalloc (a
  * plugin inside a host program that owns all device memory, a fixed memory

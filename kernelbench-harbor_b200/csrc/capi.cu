@@ -11,6 +11,10 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
              int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream);
 
+size_t w8a8_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
+int w8a8_tc(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y, int64_t M,
+            int64_t N, int64_t K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 // Rows from which the tensor-core (tcgen05) path is used.
 constexpr int64_t W4A16_TC_MIN_M = 33;
 
@@ -49,6 +53,24 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (M >= W4A16_TC_MIN_M)
     return w4a16_tc(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
   return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
+}
+
+size_t b200q_w8a8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device) {
+  if (M <= 0 || N <= 0 || K <= 0) return 256;
+  return b200q::w8a8_ws_bytes(M, N, K, device);
+}
+
+int b200q_w8a8_gemm(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y,
+                    int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace b200q;
+  if (M < 0 || N <= 0 || K <= 0) return fail(B200Q_ERR_SHAPE, "w8a8: M must be >= 0 and N, K > 0");
+  if (K % 16) return fail(B200Q_ERR_ALIGN, "w8a8: K must be a multiple of 16 (x rows must be 16-byte pitched)");
+  if (N % 32) return fail(B200Q_ERR_ALIGN, "w8a8: N must be a multiple of 32");
+  if (M > (1ll << 30) || N > (1ll << 30) || K > 130000) return fail(B200Q_ERR_SHAPE, "w8a8: size too large");
+  if (M == 0) return B200Q_OK;
+  if (!x_int8 || !w_int8 || !x_scale || !w_scale || !y) return fail(B200Q_ERR_SHAPE, "w8a8: null pointer argument");
+  return w8a8_tc(x_int8, w_int8, x_scale, w_scale, y, M, N, K, workspace, workspace_bytes,
+                 reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

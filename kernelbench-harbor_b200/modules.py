@@ -30,5 +30,14 @@ class W4A16Linear(nn.Module):
         return y.reshape(*lead, y.shape[-1])
 
 
+class W8A8Linear(nn.Module):
+    """W8A8 SmoothQuant linear: W8A8_REF.forward, generate_tasks.py:204-206.
+    x_int8:[M,K] int8; w_int8:[K,N] int8; x_scale:[M,1] fp16; w_scale:[1,N]
+    fp16; returns fp16 [M,N]."""
+
+    def forward(self, x_int8, w_int8, x_scale, w_scale):
+        return ops.w8a8_gemm(x_int8, w_int8, x_scale, w_scale)
+
+
 # the reference harness imports the replacement as ``ModelNew``
 ModelNew = W4A16Linear

@@ -96,6 +96,39 @@ def _(x, qweight, scales, zeros, group):
     return x.new_empty((x.shape[0], qweight.shape[1] * 8))
 
 
+@torch.library.custom_op("b200q::w8a8_gemm", mutates_args=())
+def w8a8_gemm(x_int8: torch.Tensor, w_int8: torch.Tensor, x_scale: torch.Tensor,
+              w_scale: torch.Tensor) -> torch.Tensor:
+    """y[M, N] = fp16((x_int8 . w_int8) * x_scale * w_scale) (W8A8_REF.forward,
+    generate_tasks.py:204-206); x_scale [M, 1] or [M], w_scale [1, N] or [N]."""
+    if not x_int8.is_cuda:
+        raise RuntimeError("b200q::w8a8_gemm runs on CUDA tensors only (no CPU implementation)")
+    if x_int8.dtype != torch.int8 or w_int8.dtype != torch.int8:
+        raise TypeError("x_int8 and w_int8 must be int8")
+    M, K = x_int8.shape
+    if w_int8.shape[0] != K:
+        raise ValueError(f"w_int8 has {w_int8.shape[0]} rows, x has K={K}")
+    N = w_int8.shape[1]
+    xs = x_scale.reshape(-1).to(torch.float16)
+    wsc = w_scale.reshape(-1).to(torch.float16)
+    if xs.numel() != M or wsc.numel() != N:
+        raise ValueError("x_scale must have M entries and w_scale N entries")
+    x_int8, w_int8, xs, wsc = (_aligned(t) for t in (x_int8, w_int8, xs, wsc))
+    y = torch.empty((M, N), dtype=torch.float16, device=x_int8.device)
+    if M == 0:
+        return y
+    L = _lib.lib()
+    ws = workspace(x_int8.device, L.b200q_w8a8_workspace_bytes(M, N, K, x_int8.device.index))
+    _lib.check(L.b200q_w8a8_gemm(x_int8.data_ptr(), w_int8.data_ptr(), xs.data_ptr(), wsc.data_ptr(),
+                                 y.data_ptr(), M, N, K, ws.data_ptr(), ws.numel(), _stream_ptr(x_int8.device)))
+    return y
+
+
+@w8a8_gemm.register_fake
+def _(x_int8, w_int8, x_scale, w_scale):
+    return x_int8.new_empty((x_int8.shape[0], w_int8.shape[1]), dtype=torch.float16)
+
+
 def device_status(device: torch.device | None = None) -> int:
     """Reads and clears the device error word of this stream's workspace
     (synchronises the stream).  0 means no kernel reported an error."""
