@@ -81,6 +81,29 @@ size_t b200q_w8a8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device);
 int b200q_w8a8_gemm(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y,
                     int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Top-2 routing of a mixture of experts (MOE_REF / FUSED_QMOE_REF routing,
+ * generate_tasks.py:171-173, 368-371): softmax of the fp32-upcast logits
+ * [T, E], the two largest (equal logits: lower expert index first), gates =
+ * renormalised pair in the logits' dtype.  Also builds the permutation: per
+ * expert e the routed tokens in ascending order in slots [offsets[e],
+ * offsets[e+1]) (slot_token [2T]), and each token's two slots (token_slot
+ * [T, 2]).  topi [T, 2] int32, gates [T, 2], offsets [E + 1].  2 <= E <= 256. */
+int b200q_moe_route(const void* logits, int64_t T, int64_t E, int dtype, int32_t* topi, void* gates,
+                    int32_t* offsets, int32_t* slot_token, int32_t* token_slot, void* stream);
+
+/* xg[s, :] = x[slot_token[s], :] for s < nslots (rows of D fp16/bf16, D % 8 == 0). */
+int b200q_moe_gather(const void* x, const int32_t* slot_token, int64_t nslots, int64_t D, void* xg, void* stream);
+
+/* h = (silu(gate.float()) * up.float()).to(dtype), elementwise over n values
+ * (the SiLU.mul of FUSED_SILU_REF, generate_tasks.py:336-337). */
+int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dtype, void* stream);
+
+/* y[t] = ye[token_slot[t,0]] * gates[t,0] + ye[token_slot[t,1]] * gates[t,1],
+ * products and sum rounded to dtype as the reference's (sel * topv).sum(1)
+ * (generate_tasks.py:377-378).  ye [2T, D], y [T, D]. */
+int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
+                      int dtype, void* stream);
+
 /* y = x . dequant(qweight, scales, zeros) for 1 <= M <= 32, with no workspace
  * argument and no allocation: for callers that cannot call cudaMalloc (a
  * plugin inside a host program that owns all device memory, a fixed memory

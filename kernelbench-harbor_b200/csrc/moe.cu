@@ -1,0 +1,230 @@
+// Quantised top-2 mixture-of-experts: routing, token permutation, SiLU.mul and
+// the gated combine.  The expert GEMMs are the W4A16 kernels of this library.
+//
+// Reference semantics (FUSED_QMOE_REF / MOE_REF, generate_tasks.py:171-178,
+// 368-378, SiLU.mul of FUSED_SILU_REF :336-337):
+//   probs = softmax(logits.float());  topv, topi = probs.topk(2)
+//   gates = (topv / topv.sum()).to(x.dtype)
+//   h_e   = (silu(gate_e.float()) * up_e.float()).to(x.dtype)
+//   y[t]  = sum_k  out_{topi[t,k]}[t] * gates[t,k]      (x.dtype products, one sum)
+// Selection compares the logits (softmax is monotonic; distinct fp16 logits give
+// distinct fp32 probabilities); equal logits: the lower expert index wins.
+//
+// Permutation: the routing kernel (one CTA, deterministic) writes, per expert e,
+// the tokens routed to it in ascending token order into slots
+// [offsets[e], offsets[e+1]), plus each token's two slot numbers.  Experts then
+// run on contiguous row blocks, and the combine reads each token's two rows.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace b200q {
+namespace moe {
+
+constexpr int ROUTE_THREADS = 1024;
+constexpr int MAX_EXPERTS = 256;
+
+template <class T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <class T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <class T>
+__global__ void __launch_bounds__(ROUTE_THREADS, 1)
+    route_kernel(const T* __restrict__ logits, int T_, int E, int32_t* __restrict__ topi, T* __restrict__ gates,
+                 int32_t* __restrict__ offsets, int32_t* __restrict__ slot_token, int32_t* __restrict__ token_slot) {
+  __shared__ int s_count[MAX_EXPERTS];
+  __shared__ int s_base[MAX_EXPERTS];
+  __shared__ int s_warp[ROUTE_THREADS / 32];
+  __shared__ int s_total;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  for (int e = tid; e < E; e += ROUTE_THREADS) s_count[e] = 0;
+  __syncthreads();
+  // pass 1: top-2 per token, gates, expert counts
+  for (int t = tid; t < T_; t += ROUTE_THREADS) {
+    const T* l = logits + (size_t)t * E;
+    float v0 = -INFINITY, v1 = -INFINITY;
+    int i0 = 0, i1 = 1;
+    for (int e = 0; e < E; ++e) {
+      const float v = to_f<T>(l[e]);
+      if (v > v0) {
+        v1 = v0;
+        i1 = i0;
+        v0 = v;
+        i0 = e;
+      } else if (v > v1) {
+        v1 = v;
+        i1 = e;
+      }
+    }
+    if (i1 == i0) i1 = i0 == 0 ? 1 : 0;  // E >= 2 guaranteed by the caller; all -inf rows
+    // softmax of the two selected entries over all E (max is v0)
+    float sum = 0.f;
+    for (int e = 0; e < E; ++e) sum += expf(to_f<T>(l[e]) - v0);
+    const float p0 = 1.f / sum, p1 = expf(v1 - v0) / sum;
+    const float tot = p0 + p1;
+    topi[2 * t] = i0;
+    topi[2 * t + 1] = i1;
+    gates[2 * t] = from_f<T>(p0 / tot);
+    gates[2 * t + 1] = from_f<T>(p1 / tot);
+    atomicAdd(&s_count[i0], 1);
+    atomicAdd(&s_count[i1], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = acc;
+      s_base[e] = acc;
+      acc += s_count[e];
+    }
+    offsets[E] = acc;
+  }
+  __syncthreads();
+  // pass 2: stable slots (ascending token order within each expert): for each
+  // expert, a block-wide exclusive scan of "token t is routed to e" per chunk
+  for (int t0 = 0; t0 < T_; t0 += ROUTE_THREADS) {
+    const int t = t0 + tid;
+    const bool valid = t < T_;
+    const int a = valid ? topi[2 * t] : -1, b = valid ? topi[2 * t + 1] : -1;
+    for (int e = 0; e < E; ++e) {
+      const bool f = (a == e) || (b == e);
+      const unsigned m = __ballot_sync(0xffffffffu, f);
+      if (lane == 0) s_warp[wid] = __popc(m);
+      __syncthreads();
+      if (tid == 0) {
+        int acc = 0;
+        for (int w = 0; w < ROUTE_THREADS / 32; ++w) {
+          const int c = s_warp[w];
+          s_warp[w] = acc;
+          acc += c;
+        }
+        s_total = acc;
+      }
+      __syncthreads();
+      if (f) {
+        const int slot = s_base[e] + s_warp[wid] + __popc(m & ((1u << lane) - 1u));
+        slot_token[slot] = t;
+        token_slot[2 * t + (a == e ? 0 : 1)] = slot;
+      }
+      __syncthreads();
+      if (tid == 0) s_base[e] += s_total;
+      __syncthreads();
+    }
+  }
+}
+
+__global__ void gather_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ slot_token, int nslots,
+                              int row16, uint4* __restrict__ xg) {
+  const int slot = blockIdx.x;
+  if (slot >= nslots) return;
+  const uint4* src = x + (size_t)slot_token[slot] * row16;
+  uint4* dst = xg + (size_t)slot * row16;
+  for (int i = threadIdx.x; i < row16; i += blockDim.x) dst[i] = src[i];
+}
+
+template <class T>
+__global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ h, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float a = to_f<T>(g[i]);
+    h[i] = from_f<T>(a / (1.f + expf(-a)) * to_f<T>(u[i]));
+  }
+}
+
+template <class T>
+__global__ void combine_kernel(const T* __restrict__ ye, const int32_t* __restrict__ token_slot,
+                               const T* __restrict__ gates, T* __restrict__ y, int D) {
+  const int t = blockIdx.x;
+  const int s0 = token_slot[2 * t], s1 = token_slot[2 * t + 1];
+  const T g0 = gates[2 * t], g1 = gates[2 * t + 1];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    // x.dtype products (one rounding each), then their sum rounded once
+    const float p0 = to_f<T>(from_f<T>(to_f<T>(ye[(size_t)s0 * D + d]) * to_f<T>(g0)));
+    const float p1 = to_f<T>(from_f<T>(to_f<T>(ye[(size_t)s1 * D + d]) * to_f<T>(g1)));
+    y[(size_t)t * D + d] = from_f<T>(p0 + p1);
+  }
+}
+
+}  // namespace moe
+}  // namespace b200q
+
+extern "C" {
+
+int b200q_moe_route(const void* logits, int64_t T, int64_t E, int dtype, int32_t* topi, void* gates,
+                    int32_t* offsets, int32_t* slot_token, int32_t* token_slot, void* stream) {
+  using namespace b200q;
+  if (T < 0 || E < 2 || E > moe::MAX_EXPERTS)
+    return fail(B200Q_ERR_SHAPE, "moe_route: need T >= 0 and 2 <= E <= 256");
+  if (dtype != B200Q_DTYPE_FP16 && dtype != B200Q_DTYPE_BF16)
+    return fail(B200Q_ERR_UNSUPPORTED, "moe_route: dtype must be fp16 or bf16");
+  if (T > (1ll << 30)) return fail(B200Q_ERR_SHAPE, "moe_route: too many tokens");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == B200Q_DTYPE_FP16)
+    moe::route_kernel<__half><<<1, moe::ROUTE_THREADS, 0, st>>>(
+        reinterpret_cast<const __half*>(logits), (int)T, (int)E, topi, reinterpret_cast<__half*>(gates), offsets,
+        slot_token, token_slot);
+  else
+    moe::route_kernel<__nv_bfloat16><<<1, moe::ROUTE_THREADS, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(logits), (int)T, (int)E, topi,
+        reinterpret_cast<__nv_bfloat16*>(gates), offsets, slot_token, token_slot);
+  return check_cuda(cudaGetLastError(), "moe_route launch");
+}
+
+int b200q_moe_gather(const void* x, const int32_t* slot_token, int64_t nslots, int64_t D, void* xg, void* stream) {
+  using namespace b200q;
+  if (nslots < 0 || D <= 0 || D % 8) return fail(B200Q_ERR_SHAPE, "moe_gather: D must be a positive multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(xg)) & 15)
+    return fail(B200Q_ERR_ALIGN, "moe_gather: pointers must be 16-byte aligned");
+  if (nslots == 0) return B200Q_OK;
+  moe::gather_kernel<<<(unsigned)nslots, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(x), slot_token, (int)nslots, (int)(D / 8), reinterpret_cast<uint4*>(xg));
+  return check_cuda(cudaGetLastError(), "moe_gather launch");
+}
+
+int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dtype, void* stream) {
+  using namespace b200q;
+  if (n < 0) return fail(B200Q_ERR_SHAPE, "silu_mul: n must be >= 0");
+  if (n == 0) return B200Q_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  if (dtype == B200Q_DTYPE_FP16)
+    moe::silu_mul_kernel<__half><<<blocks, 256, 0, st>>>(reinterpret_cast<const __half*>(gate),
+                                                          reinterpret_cast<const __half*>(up),
+                                                          reinterpret_cast<__half*>(h), (size_t)n);
+  else if (dtype == B200Q_DTYPE_BF16)
+    moe::silu_mul_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(gate),
+                                                                 reinterpret_cast<const __nv_bfloat16*>(up),
+                                                                 reinterpret_cast<__nv_bfloat16*>(h), (size_t)n);
+  else
+    return fail(B200Q_ERR_UNSUPPORTED, "silu_mul: dtype must be fp16 or bf16");
+  return check_cuda(cudaGetLastError(), "silu_mul launch");
+}
+
+int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
+                      int dtype, void* stream) {
+  using namespace b200q;
+  if (T < 0 || D <= 0) return fail(B200Q_ERR_SHAPE, "moe_combine: T >= 0, D > 0");
+  if (T == 0) return B200Q_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == B200Q_DTYPE_FP16)
+    moe::combine_kernel<__half><<<(unsigned)T, 256, 0, st>>>(reinterpret_cast<const __half*>(ye), token_slot,
+                                                              reinterpret_cast<const __half*>(gates),
+                                                              reinterpret_cast<__half*>(y), (int)D);
+  else if (dtype == B200Q_DTYPE_BF16)
+    moe::combine_kernel<__nv_bfloat16><<<(unsigned)T, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(ye), token_slot, reinterpret_cast<const __nv_bfloat16*>(gates),
+        reinterpret_cast<__nv_bfloat16*>(y), (int)D);
+  else
+    return fail(B200Q_ERR_UNSUPPORTED, "moe_combine: dtype must be fp16 or bf16");
+  return check_cuda(cudaGetLastError(), "moe_combine launch");
+}
+
+}  // extern "C"

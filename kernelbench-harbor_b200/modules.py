@@ -39,5 +39,41 @@ class W8A8Linear(nn.Module):
         return ops.w8a8_gemm(x_int8, w_int8, x_scale, w_scale)
 
 
+class QuantizedMoE(nn.Module):
+    """Quantised top-2 MoE FFN (the benchmark's Mixtral-shaped composite):
+    routing of FUSED_QMOE_REF (generate_tasks.py:368-371), per expert
+    h = SiLU(x . Wg) * (x . Wu) (FUSED_SILU_REF's SiLU.mul, :336-337) and
+    out = h . Wd with W4A16 weights, then the gated combine of :377-378.
+
+    forward(x [T, D], router_logits [T, E],
+            gate_q [E, D, H/8], gate_s [E, D/g, H], gate_z,
+            up_q, up_s, up_z            (same shapes as gate),
+            down_q [E, H, D/8], down_s [E, H/g, D], down_z) -> [T, D]
+
+    Experts run one after another on contiguous row blocks of the routed
+    tokens (the routing kernel groups them); the expert row counts are read on
+    the host once per call to size those launches."""
+
+    def forward(self, x, router_logits, gate_q, gate_s, gate_z, up_q, up_s, up_z, down_q, down_s, down_z):
+        T, D = x.shape
+        E = router_logits.shape[1]
+        g = gate_q.shape[1] // gate_s.shape[1]
+        gd = down_q.shape[1] // down_s.shape[1]
+        topi, gates, offsets, slot_token, token_slot = ops.moe_route(router_logits.to(x.dtype))
+        xg = ops.moe_gather(x, slot_token)
+        offs = offsets.cpu().tolist()
+        ye = torch.empty((2 * T, D), dtype=x.dtype, device=x.device)
+        for e in range(E):
+            a, b = offs[e], offs[e + 1]
+            if b == a:
+                continue
+            rows = xg[a:b]
+            hg = ops.w4a16_gemm(rows, gate_q[e], gate_s[e], gate_z[e], g)
+            hu = ops.w4a16_gemm(rows, up_q[e], up_s[e], up_z[e], g)
+            h = ops.silu_mul(hg, hu)
+            ye[a:b] = ops.w4a16_gemm(h, down_q[e], down_s[e], down_z[e], gd)
+        return ops.moe_combine(ye, token_slot, gates)
+
+
 # the reference harness imports the replacement as ``ModelNew``
 ModelNew = W4A16Linear

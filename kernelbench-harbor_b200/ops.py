@@ -129,6 +129,52 @@ def _(x_int8, w_int8, x_scale, w_scale):
     return x_int8.new_empty((x_int8.shape[0], w_int8.shape[1]), dtype=torch.float16)
 
 
+def moe_route(router_logits: torch.Tensor):
+    """Top-2 routing + expert-grouped permutation (see include/b200q.h).
+    Returns topi [T,2] int32, gates [T,2] (logits dtype), offsets [E+1] int32,
+    slot_token [2T] int32, token_slot [T,2] int32."""
+    if not router_logits.is_cuda:
+        raise RuntimeError("b200q moe_route runs on CUDA tensors only")
+    lg = _aligned(router_logits)
+    T, E = lg.shape
+    dev = lg.device
+    topi = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    gates = torch.empty((T, 2), dtype=lg.dtype, device=dev)
+    offsets = torch.empty((E + 1,), dtype=torch.int32, device=dev)
+    slot_token = torch.empty((2 * T,), dtype=torch.int32, device=dev)
+    token_slot = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    _lib.check(_lib.lib().b200q_moe_route(lg.data_ptr(), T, E, _dtype_code(lg.dtype), topi.data_ptr(),
+                                          gates.data_ptr(), offsets.data_ptr(), slot_token.data_ptr(),
+                                          token_slot.data_ptr(), _stream_ptr(dev)))
+    return topi, gates, offsets, slot_token, token_slot
+
+
+def moe_gather(x: torch.Tensor, slot_token: torch.Tensor) -> torch.Tensor:
+    x = _aligned(x)
+    xg = torch.empty((slot_token.numel(), x.shape[1]), dtype=x.dtype, device=x.device)
+    _lib.check(_lib.lib().b200q_moe_gather(x.data_ptr(), slot_token.data_ptr(), slot_token.numel(), x.shape[1],
+                                           xg.data_ptr(), _stream_ptr(x.device)))
+    return xg
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    gate, up = gate.contiguous(), up.contiguous()
+    h = torch.empty_like(gate)
+    _lib.check(_lib.lib().b200q_silu_mul(gate.data_ptr(), up.data_ptr(), h.data_ptr(), gate.numel(),
+                                         _dtype_code(gate.dtype), _stream_ptr(gate.device)))
+    return h
+
+
+def moe_combine(ye: torch.Tensor, token_slot: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
+    ye = ye.contiguous()
+    T = token_slot.shape[0]
+    y = torch.empty((T, ye.shape[1]), dtype=ye.dtype, device=ye.device)
+    _lib.check(_lib.lib().b200q_moe_combine(ye.data_ptr(), token_slot.data_ptr(), gates.contiguous().data_ptr(),
+                                            y.data_ptr(), T, ye.shape[1], _dtype_code(ye.dtype),
+                                            _stream_ptr(ye.device)))
+    return y
+
+
 def device_status(device: torch.device | None = None) -> int:
     """Reads and clears the device error word of this stream's workspace
     (synchronises the stream).  0 means no kernel reported an error."""

@@ -105,3 +105,15 @@ def check_w4a16(y, x, qweight, scales, zeros, group):
     else:
         torch.testing.assert_close(y.float(), torch_ref_module(x, qweight, scales, zeros, group), **TOL)
         torch.testing.assert_close(y.float(), ref32, rtol=5e-2, atol=5e-2)
+
+
+def torch_dequant_fp32(qweight, scales, zeros, group):
+    """fp32 weight [K, N] = (unpack(qweight) - z) * s (generate_tasks.py:55-61 in fp32)."""
+    K = qweight.shape[0]
+    N = qweight.shape[1] * 8
+    shifts = torch.arange(0, 32, 4, device=qweight.device, dtype=torch.int32)
+    w = ((qweight.unsqueeze(-1) >> shifts) & 0xF).reshape(K, N).float()
+    g = K // group
+    s = scales.float().reshape(g, 1, N).expand(g, group, N).reshape(K, N)
+    z = zeros.float().reshape(g, 1, N).expand(g, group, N).reshape(K, N)
+    return (w - z) * s
