@@ -104,6 +104,18 @@ int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dty
 int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
                       int dtype, void* stream);
 
+/* Bytes of zero-initialised workspace b200q_mxfp8_gemm needs for this shape. */
+size_t b200q_mxfp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device);
+
+/* MXFP8 block-scaled GEMM: y[M, N] = fp16(A_deq . B_deq^T), A [M, K] and B
+ * [N, K] e4m3 codes (K-major), scales_a [M, K/32] and scales_b [N, K/32] E8M0
+ * (OCP MX v1.0, bias 127), fp32 accumulation.  The reference has no MX module;
+ * its nearest operator is FP8_REF.forward (generate_tasks.py:226-229, a
+ * weight-only fp8 GEMM with fp16 block scales).  Requirements: K % 128 == 0,
+ * N % 32 == 0, 16-byte aligned A/B/y, 4-byte aligned scales. */
+int b200q_mxfp8_gemm(const void* a, const void* scales_a, const void* b, const void* scales_b, void* y, int64_t M,
+                     int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* y = x . dequant(qweight, scales, zeros) for 1 <= M <= 32, with no workspace
  * argument and no allocation: for callers that cannot call cudaMalloc (a
  * plugin inside a host program that owns all device memory, a fixed memory

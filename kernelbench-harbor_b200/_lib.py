@@ -36,6 +36,9 @@ SIGNATURES = {
     "b200q_w8a8_workspace_bytes": (_c_sz, [_c_i64, _c_i64, _c_i64, ctypes.c_int]),
     "b200q_w8a8_gemm": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_sz,
                                        _c_vp]),
+    "b200q_mxfp8_workspace_bytes": (_c_sz, [_c_i64, _c_i64, _c_i64, ctypes.c_int]),
+    "b200q_mxfp8_gemm": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_sz,
+                                        _c_vp]),
     "b200q_moe_route": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                        _c_vp]),
     "b200q_moe_gather": (ctypes.c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),

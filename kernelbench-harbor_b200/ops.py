@@ -129,6 +129,27 @@ def _(x_int8, w_int8, x_scale, w_scale):
     return x_int8.new_empty((x_int8.shape[0], w_int8.shape[1]), dtype=torch.float16)
 
 
+def mxfp8_gemm(a: torch.Tensor, scales_a: torch.Tensor, b: torch.Tensor, scales_b: torch.Tensor) -> torch.Tensor:
+    """y[M, N] = fp16(A_deq . B_deq^T) for OCP-MX e4m3 operands (codes as uint8 or
+    float8_e4m3fn [M, K] / [N, K], E8M0 scales uint8 [M, K/32] / [N, K/32])."""
+    if not a.is_cuda:
+        raise RuntimeError("b200q mxfp8_gemm runs on CUDA tensors only")
+    a, b = (t.view(torch.uint8) if t.dtype != torch.uint8 else t for t in (a, b))
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K or scales_a.shape != (M, K // 32) or scales_b.shape != (N, K // 32):
+        raise ValueError("mxfp8_gemm: shapes must be A [M,K], B [N,K], scales [*, K/32]")
+    a, b, scales_a, scales_b = (_aligned(t) for t in (a, b, scales_a, scales_b))
+    y = torch.empty((M, N), dtype=torch.float16, device=a.device)
+    if M == 0:
+        return y
+    L = _lib.lib()
+    ws = workspace(a.device, L.b200q_mxfp8_workspace_bytes(M, N, K, a.device.index))
+    _lib.check(L.b200q_mxfp8_gemm(a.data_ptr(), scales_a.data_ptr(), b.data_ptr(), scales_b.data_ptr(),
+                                  y.data_ptr(), M, N, K, ws.data_ptr(), ws.numel(), _stream_ptr(a.device)))
+    return y
+
+
 def moe_route(router_logits: torch.Tensor):
     """Top-2 routing + expert-grouped permutation (see include/b200q.h).
     Returns topi [T,2] int32, gates [T,2] (logits dtype), offsets [E+1] int32,
