@@ -123,23 +123,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------------------- scale factors -> TMEM (warps 2..5)
     const int qd = warp & 3;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    for (int it = 0; it < nk; ++it) {
-      const int s = it % STAGES;
-      if (it >= STAGES && !mbar_wait(&sf_empty[s], ((it / STAGES) - 1) & 1, status)) {
-        s_err = 1;
-        break;
-      }
-      const int wcol = (k_begin + it);  // scale word column: K-blocks 4*wcol .. 4*wcol+3
-      uint32_t ra[4], rb[8];
+    // Scale words are prefetched SF_AHEAD stages ahead in registers: their
+    // global loads do not depend on the TMEM slot being free, only the stores do.
+    constexpr int SF_AHEAD = 3;
+    uint32_t pre[SF_AHEAD][12];
+    auto load_sf = [&](int it, uint32_t* w) {
+      const int wcol = k_begin + it;  // scale word column: K-blocks 4*wcol .. 4*wcol+3
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int r = m0 + 32 * j + lane;
-        ra[j] = r < M ? sfa[(size_t)r * kw + wcol] : 0u;
+        w[j] = (it < nk && r < M) ? __ldg(sfa + (size_t)r * kw + wcol) : 0u;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int r = n0 + 32 * j + lane;
-        rb[j] = r < N ? sfb[(size_t)r * kw + wcol] : 0u;
+        w[4 + j] = (it < nk && r < N) ? __ldg(sfb + (size_t)r * kw + wcol) : 0u;
+      }
+    };
+#pragma unroll
+    for (int d = 0; d < SF_AHEAD; ++d) load_sf(d, pre[d]);
+    for (int it = 0; it < nk; ++it) {
+      const int s = it % STAGES;
+      uint32_t cur[12];
+#pragma unroll
+      for (int i = 0; i < 12; ++i) cur[i] = pre[0][i];
+#pragma unroll
+      for (int d = 0; d + 1 < SF_AHEAD; ++d)
+#pragma unroll
+        for (int i = 0; i < 12; ++i) pre[d][i] = pre[d + 1][i];
+      load_sf(it + SF_AHEAD, pre[SF_AHEAD - 1]);
+      if (it >= STAGES && !mbar_wait(&sf_empty[s], ((it / STAGES) - 1) & 1, status)) {
+        s_err = 1;
+        break;
       }
       // one K-block per MMA: byte kk of each row's word goes to byte 0 of that
       // MMA's scale columns
@@ -147,9 +162,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int kk = 0; kk < BK / 32; ++kk) {
         uint32_t ka[4], kb_[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) ka[j] = (ra[j] >> (8 * kk)) & 0xFFu;
+        for (int j = 0; j < 4; ++j) ka[j] = (cur[j] >> (8 * kk)) & 0xFFu;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) kb_[j] = (rb[j] >> (8 * kk)) & 0xFFu;
+        for (int j = 0; j < 8; ++j) kb_[j] = (cur[4 + j] >> (8 * kk)) & 0xFFu;
         const uint32_t sf = tmem + SF_COL0 + s * SF_STRIDE + kk * SF_MMA;
         tmem_st4(sf + lane_base, ka);
         tmem_st8(sf + 4 + lane_base, kb_);
