@@ -264,6 +264,62 @@ def run_ours(args, world, rank, device, peaks):
     return sweep, e2e, sampler.summary()
 
 
+def run_siblings(device, steps, warmup, sampler):
+    """The sibling configurations of the benchmark, each timed like the sweep
+    (CUDA graph of `steps` calls over rotating input sets, CUDA events):
+    W8A8 SmoothQuant M=16/512, MXFP8 M=128/4096, quantised top-2 MoE T=512."""
+    from kernelbench_harbor_b200 import ops
+    from kernelbench_harbor_b200.modules import QuantizedMoE
+    from kernelbench_harbor_b200.mx import quantize_mxfp8
+    from kernelbench_harbor_b200.quant import smoothquant_inputs
+    peaks = load_peaks()
+    out = {}
+    K, N = K_DIM, N_DIM
+    for M in (16, 512):
+        sets = [[t.to(device) for t in smoothquant_inputs(M, K, N, seed=100 + i)[:4]] for i in range(4)]
+        us = time_calls(lambda i: ops.w8a8_gemm(*sets[i]), 4, steps, warmup, 1, sampler, True) * 1e3
+        b = M * K + K * N + 2 * M + 2 * N + 2 * M * N
+        out[f"w8a8_m{M}"] = {"us_per_call": round(us, 3), "GB_s": round(b / us / 1e3, 1),
+                             "TOPS": round(2 * M * N * K / us / 1e6, 1),
+                             "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4)}
+        del sets
+    for M in (128, 4096):
+        nset = 2 if M > 1024 else 4
+        sets = []
+        for i in range(nset):
+            g = torch.Generator().manual_seed(200 + i)
+            a = quantize_mxfp8(torch.randn(M, K, generator=g).half())
+            bq = quantize_mxfp8((torch.randn(N, K, generator=g) * 0.02).half())
+            sets.append([a[0].to(device), a[1].to(device), bq[0].to(device), bq[1].to(device)])
+        us = time_calls(lambda i: ops.mxfp8_gemm(*sets[i]), nset, steps, warmup, 1, sampler, True) * 1e3
+        b = M * K + N * K + (M + N) * (K // 32) + 2 * M * N
+        out[f"mxfp8_m{M}"] = {"us_per_call": round(us, 3), "GB_s": round(b / us / 1e3, 1),
+                              "TFLOP_s": round(2 * M * N * K / us / 1e6, 1),
+                              "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4)}
+        del sets
+    # MoE: Mixtral shape, one input set (its 8 experts x 3 W4A16 weights = 749 MB > L2)
+    T, D, H, E = 512, 4096, 14336, 8
+    g = torch.Generator(device=device).manual_seed(300)
+    x = torch.randn(T, D, generator=g, device=device).half()
+    logits = (x.float() @ (torch.randn(E, D, generator=g, device=device) * 0.02).t()).half()
+    ws = []
+    for (kk, nn) in ((D, H), (D, H), (H, D)):
+        q, s_, z = [], [], []
+        for e in range(E):
+            qe, se, ze = make_weights(400 + 10 * e + len(ws), device, K=kk, N=nn)
+            q.append(qe), s_.append(se), z.append(ze)
+        ws += [torch.stack(q), torch.stack(s_), torch.stack(z)]
+    moe = QuantizedMoE()
+    msteps = max(3, min(steps, 20))
+    us = time_calls(lambda i: moe(x, logits, *ws), 1, msteps, warmup, 1, sampler, False) * 1e3
+    fl = T * 2 * 3 * 2 * D * H
+    wb = E * 3 * (D * H // 2 + 2 * (D // GROUP) * H * 2)
+    out["moe_top2_t512"] = {"us_per_call": round(us, 1), "TFLOP_s": round(fl / us / 1e6, 1),
+                            "weight_GB_s": round(wb / us / 1e3, 1), "steps": msteps,
+                            "timing": "eager launches (host reads expert row counts each call)"}
+    return out
+
+
 # ---------------------------------------------------------------------------- CPU legs
 def cpu_reference_time(M, steps, warmup, budget_s=0.25):
     """Median seconds of one full call of the reference op sequence on the host
@@ -304,6 +360,7 @@ def main():
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=list(SWEEP_M))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-siblings", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -335,6 +392,9 @@ def main():
     device = torch.device("cuda", torch.cuda.current_device())
     peaks = load_peaks()
     sweep, e2e, clocks = run_ours(args, world, rank, device, peaks)
+    siblings = None
+    if world == 1 and not args.no_siblings:
+        siblings = run_siblings(device, args.steps, args.warmup, ClockSampler(device.index))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -367,7 +427,7 @@ def main():
                 "config": {"workload": workload,
                            "parallelism": f"N-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
                            "l2": head["l2"]},
-                "roofline": roof, "sweep": {str(k): v for k, v in sweep.items()},
+                "roofline": roof, "sweep": {str(k): v for k, v in sweep.items()}, "siblings": siblings,
                 "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
