@@ -10,8 +10,9 @@
 //
 // One CTA computes a 128 x 256 or 256 x 256 output tile (MB = 1 or 2 blocks
 // of 128 rows sharing every dequantised weight tile, one TMEM accumulator of
-// 256 columns each) over a K range (split-K only when the tile grid cannot
-// fill the SMs).  Warp roles:
+// 256 columns each) over a K range.  Split-K (only when the tile grid cannot
+// fill the SMs) launches the K ranges of a tile as one thread-block cluster and
+// reduces the partial tiles through distributed shared memory.  Warp roles:
 //   warp 0      weight producer: per 64-deep K stage, TMA of the packed weight
 //               tile [64 x 32 words] and the stage's scale / zero rows into a
 //               ring whose slots free as soon as they are dequantised;
@@ -44,15 +45,25 @@ constexpr uint32_t WQ_BYTES = BK * (BN / 8) * 4;   // 8 KB
 constexpr uint32_t SZ_BYTES = 2 * BN * 2;          // up to 2 scale rows per stage (group 32)
 constexpr uint32_t B_BYTES = BK * BN * 2;          // 32 KB
 constexpr int HEADER_BYTES = 256;
-constexpr int MAX_SPLITS = 16;
+constexpr int MAX_SPLITS = 8;  // portable cluster size
+
+#ifndef B200Q_TC1_SX
+#define B200Q_TC1_SX 4
+#endif
+#ifndef B200Q_TC1_SW
+#define B200Q_TC1_SW 6
+#endif
+#ifndef B200Q_TC1_S2
+#define B200Q_TC1_S2 3
+#endif
 
 // MB = number of 128-row blocks of x per CTA sharing each dequantised B tile
 // (1: 128 x 256 tile, 256 TMEM columns; 2: 256 x 256 tile, all 512 columns).
 template <int MB>
 struct Cfg {
-  static constexpr int SX = MB == 1 ? 4 : 3;  // x ring (held until the MMAs of the stage complete)
-  static constexpr int SW = MB == 1 ? 6 : 4;  // packed-weight + scale/zero ring (held until dequantised)
-  static constexpr int S2 = MB == 1 ? 3 : 2;  // dequantised-B ring
+  static constexpr int SX = MB == 1 ? B200Q_TC1_SX : 3;  // x ring (held until the MMAs of the stage complete)
+  static constexpr int SW = MB == 1 ? B200Q_TC1_SW : 4;  // packed-weight + scale/zero ring (held until dequantised)
+  static constexpr int S2 = MB == 1 ? B200Q_TC1_S2 : 2;  // dequantised-B ring
   static constexpr uint32_t X_BYTES = MB * XB_BYTES;
   static constexpr uint32_t OFF_X = 0;
   static constexpr uint32_t OFF_B = OFF_X + SX * X_BYTES;
@@ -170,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* b_empty = b_full + S2;
   uint64_t* acc_full = b_empty + S2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  __shared__ int s_err, s_last;
+  __shared__ int s_err;
 
   int* status = reinterpret_cast<int*>(ws);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -319,9 +330,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int part = dw >> 2;  // which of the NDQ/4 column ranges of this quadrant
       constexpr int COLS = MB * BN / (NDQ / 4);  // lies within one accumulator
       const int acc = (part * COLS) / BN;
-      const int row = m0 + acc * BM + qd * 32 + lane;
+      const int trow = acc * BM + qd * 32 + lane;  // row within the CTA tile
+      const int row = m0 + trow;
       T* y = reinterpret_cast<T*>(y_);
-      float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
 #pragma unroll 1
       for (int c0 = 0; c0 < COLS; c0 += 32) {
         const int tcol = part * COLS + c0;  // TMEM column: accumulator acc, column tcol % BN
@@ -332,9 +343,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         float v[32];
 #pragma unroll
         for (int p = 0; p < 32; ++p) v[(p & ~7) | slot_col(p & 7)] = __uint_as_float(r[p]);
-        const int col = n0 + cslot;
-        if (row < M && col < N) {
-          if (splits == 1) {
+        if (splits == 1) {
+          const int col = n0 + cslot;
+          if (row < M && col < N) {
             uint32_t packed[16];
 #pragma unroll
             for (int p = 0; p < 16; ++p) {
@@ -347,11 +358,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int p = 0; p < 4; ++p)
               dst[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
-          } else {
-            float4* dst = reinterpret_cast<float4*>(acc_ws + (size_t)row * N + col);
-#pragma unroll
-            for (int p = 0; p < 8; ++p)
-              atomicAdd(dst + p, make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]));
           }
         }
       }
@@ -360,32 +366,61 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (splits > 1 && !s_err) {
-    // split-K: the last CTA of this output tile converts the fp32 sum and
-    // clears it (and the ticket), returning the workspace to zero.
-    __threadfence();
-    __syncthreads();
-    int* tickets = reinterpret_cast<int*>(ws + HEADER_BYTES + (size_t)M * N * 4);
-    const int tile_id = m_tile * gridDim.x + n_tile;
-    if (threadIdx.x == 0) s_last = atomicAdd(&tickets[tile_id], 1) == splits - 1;
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      float* acc_ws = reinterpret_cast<float*>(ws + HEADER_BYTES);
-      T* y = reinterpret_cast<T*>(y_);
-      const int rows = min(BM * MB, M - m0), cols = min(BN, N - n0);
-      for (int e = threadIdx.x * 4; e < rows * cols; e += THREADS * 4) {
-        const int rr = e / cols, cc = e % cols;  // cols % 32 == 0: a float4 never straddles rows
-        float4* src = reinterpret_cast<float4*>(acc_ws + (size_t)(m0 + rr) * N + n0 + cc);
-        const float4 a = __ldcg(src);
-        T* d = y + (size_t)(m0 + rr) * N + n0 + cc;
-        d[0] = (T)a.x;
-        d[1] = (T)a.y;
-        d[2] = (T)a.z;
-        d[3] = (T)a.w;
-        __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+  if (splits > 1) {
+    // split-K across the CTAs of this cluster (one per K range): row block
+    // [rank * R, rank * R + R) of the tile is owned by cluster rank `rank`.
+    // Each CTA sends its partial rows to the owners' shared memory (the
+    // pipeline buffers, free once every CTA passed the first cluster barrier),
+    // then every owner sums the S partials in rank order and writes y: the
+    // result does not depend on timing, and no global workspace is used.
+    const uint32_t S = (uint32_t)splits, R = BM / S;
+    const uint32_t rank = cluster_ctarank();
+    cluster_sync();
+    if (warp >= W_DQ0 && !s_err) {
+      tc_fence_after();
+      const int dw = warp - W_DQ0;
+      const int qd = warp & 3, part = dw >> 2;
+      constexpr int COLS = BN / (NDQ / 4);
+      const uint32_t trow = qd * 32 + lane;
+      const uint32_t owner = trow / R, lr = trow % R;
+      const uint32_t base = map_shared_rank(smem_u32(smem), owner) + ((rank * R + lr) * BN) * 4;
+#pragma unroll 1
+      for (int c0 = 0; c0 < COLS; c0 += 32) {
+        const int cslot = part * COLS + c0;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + cslot, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int p = 0; p < 32; ++p) v[(p & ~7) | slot_col(p & 7)] = __uint_as_float(r[p]);
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          st_cluster_v4(base + (cslot + 4 * p) * 4, v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
       }
-      if (threadIdx.x == 0) tickets[tile_id] = 0;
+    }
+    cluster_sync();
+    if (!s_err) {
+      const float* buf = reinterpret_cast<const float*>(smem);
+      T* y = reinterpret_cast<T*>(y_);
+      for (int e = threadIdx.x * 4; e < (int)(R * BN); e += THREADS * 4) {
+        const int lr = e / BN, c = e % BN;
+        float4 acc4 = reinterpret_cast<const float4*>(buf + lr * BN + c)[0];
+        for (uint32_t src = 1; src < S; ++src) {
+          const float4 p4 = reinterpret_cast<const float4*>(buf + (src * R + lr) * BN + c)[0];
+          acc4.x += p4.x;
+          acc4.y += p4.y;
+          acc4.z += p4.z;
+          acc4.w += p4.w;
+        }
+        const int row = m0 + (int)(rank * R) + lr, col = n0 + c;
+        if (row < M && col < N) {
+          T* d = y + (size_t)row * N + col;
+          d[0] = (T)acc4.x;
+          d[1] = (T)acc4.y;
+          d[2] = (T)acc4.z;
+          d[3] = (T)acc4.w;
+        }
+      }
     }
   }
   if (warp == W_MMA) {
@@ -393,6 +428,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
+
 
 struct Plan {
   int mb, tiles_m, tiles_n, splits;
@@ -408,12 +444,15 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   p.mb = tiles2 >= sms ? 2 : 1;
   p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
   const int nk = (int)((K + BK - 1) / BK);
-  int sp = sms / (p.tiles_m * p.tiles_n);
-  if (sp < 1) sp = 1;
-  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
-  if (sp > nk / 4) sp = nk / 4 > 0 ? nk / 4 : 1;  // keep >= 4 stages per split
+  // split-K: the K ranges of a tile form one thread-block cluster (a power of
+  // two <= 8 so row blocks of 128 / splits split evenly), as many as the SMs
+  // allow, keeping >= 4 stages per range
+  const int fill = sms / (p.tiles_m * p.tiles_n);
+  int sp = 1;
+  while (sp * 2 <= MAX_SPLITS && sp * 2 <= fill && sp * 2 <= nk / 4) sp *= 2;
+  if (p.mb == 2) sp = 1;
   p.splits = sp;
-  p.ws_bytes = HEADER_BYTES + (sp > 1 ? (size_t)M * N * 4 + (size_t)p.tiles_m * p.tiles_n * 4 : 0);
+  p.ws_bytes = HEADER_BYTES;
   return p;
 }
 
@@ -427,7 +466,7 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
              int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream) {
   using namespace tc;
-  const Plan p = plan(M, N, K, num_sms(-1));
+  Plan p = plan(M, N, K, num_sms(-1));
   if (!workspace || workspace_bytes < p.ws_bytes)
     return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(p.ws_bytes) + " bytes required");
   const CUtensorMapDataType h16 = CU_TENSOR_MAP_DATA_TYPE_UINT16;
@@ -448,9 +487,41 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
   const uint32_t smem = p.mb == 2 ? Cfg<2>::SMEM : Cfg<1>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 tc)");
+  // a cluster of `splits` CTAs (one SM each) must fit in one GPC: shrink the
+  // cluster until every cluster of the grid is resident at once
+  while (p.splits > 1) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(p.tiles_n, p.tiles_m, p.splits);
+    q.blockDim = dim3(THREADS);
+    q.dynamicSmemBytes = smem;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 1;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = (unsigned)p.splits;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, kern, &q) == cudaSuccess && active >= p.tiles_m * p.tiles_n) break;
+    cudaGetLastError();
+    p.splits /= 2;
+  }
   dim3 grid(p.tiles_n, p.tiles_m, p.splits);
-  kern<<<grid, THREADS, smem, stream>>>(tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
-                                        reinterpret_cast<uint8_t*>(workspace));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
+                         reinterpret_cast<uint8_t*>(workspace));
+  if (e != cudaSuccess) return check_cuda(e, "w4a16 tc launch");
   return check_cuda(cudaGetLastError(), "w4a16 tc launch");
 }
 
