@@ -72,3 +72,71 @@ class ColumnShardedW4A16(nn.Module):
         if world == 1:
             return y_local
         return gather_columns(y_local, world, self.pg)
+
+
+class ExpertParallelMoE(nn.Module):
+    """Expert-parallel quantised top-2 MoE: rank r of P holds experts
+    [r*E/P, (r+1)*E/P) and its own T/P tokens (data parallel).  Per call:
+      1. route the local tokens (top-2 over all E experts);
+      2. all-to-all of per-destination row counts, then of the token rows
+         (each (token, k) pair goes to the rank owning its expert);
+      3. each rank runs its experts on the rows it received;
+      4. reverse all-to-all of the expert outputs, then the gated combine of
+         each token's two rows on its home rank.
+    The reference MoE is dense and single-GPU (generate_tasks.py:368-378); this
+    is the benchmark's expert-parallel configuration (one expert per GPU at 8).
+
+    ``route``, ``expert`` and ``combine`` are injectable so the exchange logic
+    runs on CPU ranks in tests; by default they are the library's CUDA ops."""
+
+    def __init__(self, n_experts: int, process_group: Optional[dist.ProcessGroup] = None,
+                 route: Optional[Callable] = None, expert: Optional[Callable] = None,
+                 combine: Optional[Callable] = None):
+        super().__init__()
+        self.E = n_experts
+        self.pg = process_group
+        if route is None or combine is None:
+            from . import ops
+            route = route or (lambda logits: ops.moe_route(logits)[:2])
+            combine = combine or ops.moe_combine
+        self.route = route
+        self.expert = expert
+        self.combine = combine
+
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor, local_weights) -> torch.Tensor:
+        """x [T_local, D], router_logits [T_local, E]; local_weights is what
+        ``expert(e_local, rows, local_weights)`` needs for this rank's experts."""
+        P = dist.get_world_size(self.pg)
+        r = dist.get_rank(self.pg)
+        E, T, D = self.E, x.shape[0], x.shape[1]
+        epr = E // P
+        topi, gates = self.route(router_logits)
+        topi = topi.long()
+        # (token, k) pairs sorted by destination rank, then expert, then token
+        pair_e = topi.reshape(-1)
+        pair_t = torch.arange(T, device=x.device).repeat_interleave(2)
+        order = torch.argsort(pair_e * (T + 1) + pair_t, stable=True)
+        dest = pair_e[order] // epr
+        send_counts = torch.bincount(dest, minlength=P)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.pg)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        send_rows = x[pair_t[order]].contiguous()
+        send_eid = pair_e[order].to(torch.int32).contiguous()
+        recv_rows = x.new_empty((sum(rc), D))
+        recv_eid = torch.empty((sum(rc),), dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=self.pg)
+        dist.all_to_all_single(recv_eid, send_eid, rc, sc, group=self.pg)
+        # local experts on their rows
+        out = torch.empty_like(recv_rows)
+        for el in range(epr):
+            sel = torch.nonzero(recv_eid == r * epr + el).flatten()
+            if sel.numel():
+                out[sel] = self.expert(el, recv_rows[sel].contiguous(), local_weights)
+        # return trip, then undo the sort: row j of `back` is pair order[j]
+        back = x.new_empty((sum(sc), D))
+        dist.all_to_all_single(back, out, sc, rc, group=self.pg)
+        ye = torch.empty((2 * T, D), dtype=x.dtype, device=x.device)
+        ye[order] = back
+        token_slot = torch.arange(2 * T, device=x.device, dtype=torch.int32).reshape(T, 2)
+        return self.combine(ye, token_slot, gates)

@@ -64,3 +64,61 @@ def test_shard_bounds_errors():
     with pytest.raises(ValueError):
         parallel.shard_bounds(48 * 3, 3, 0)
     assert parallel.shard_bounds(4096, 8, 7) == (3584, 4096)
+
+
+def _ep_worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kernelbench_harbor_b200 import parallel
+        from oracle import moe as om
+        E, T, D = 4, 12, 8
+        g = torch.Generator().manual_seed(11)
+        xs = torch.randn(world * T, D, generator=g)
+        logits = torch.randn(world * T, E, generator=g)
+        mats = torch.randn(E, D, D, generator=g)
+
+        def route(lg):
+            ti, ga = om.route(lg.numpy())
+            return torch.from_numpy(ti), torch.from_numpy(ga)
+
+        def expert(el, rows, w):
+            return rows @ w[el]
+
+        def combine(ye, ts, ga):
+            return ye[ts[:, 0].long()] * ga[:, :1] + ye[ts[:, 1].long()] * ga[:, 1:]
+
+        epr = E // world
+        local_w = mats[rank * epr:(rank + 1) * epr]
+        mod = parallel.ExpertParallelMoE(E, route=route, expert=expert, combine=combine)
+        y = mod(xs[rank * T:(rank + 1) * T], logits[rank * T:(rank + 1) * T], local_w)
+        out.put((rank, y.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_matches_dense():
+    from oracle import moe as om
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q_out.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    E, T, D = 4, 12, 8
+    g = torch.Generator().manual_seed(11)
+    xs = torch.randn(2 * T, D, generator=g)
+    logits = torch.randn(2 * T, E, generator=g)
+    mats = torch.randn(E, D, D, generator=g)
+    ti, ga = om.route(logits.numpy())
+    ref = np.zeros((2 * T, D), dtype=np.float32)
+    for t in range(2 * T):
+        for k in range(2):
+            ref[t] += ga[t, k] * (xs[t].numpy() @ mats[ti[t, k]].numpy())
+    y = np.concatenate([res[0], res[1]])
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5)
