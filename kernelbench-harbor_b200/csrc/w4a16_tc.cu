@@ -437,11 +437,13 @@ struct Plan {
 
 Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   Plan p;
-  // 256-row tiles halve the dequantisation per FLOP; used when they alone
-  // give at least one CTA per SM (otherwise 128-row tiles fill the GPU better)
+  // 256-row tiles halve the dequantisation per FLOP but cost ~1.35x a 128-row
+  // tile (measured): pick the tile height with fewer estimated wave-times
   p.tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t tiles1 = ((M + BM - 1) / BM) * p.tiles_n;
   const int64_t tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * p.tiles_n;
-  p.mb = tiles2 >= sms ? 2 : 1;
+  const double t1 = (double)((tiles1 + sms - 1) / sms), t2 = 1.35 * (double)((tiles2 + sms - 1) / sms);
+  p.mb = (M > BM && t2 < t1) ? 2 : 1;
   p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
   const int nk = (int)((K + BK - 1) / BK);
   // split-K: the K ranges of a tile form one thread-block cluster (a power of
