@@ -10,9 +10,11 @@ benchmark's compute-bound configuration, x fp16 [4096, 14336] . W [14336, 4096]
 U{0..15}); the other M values are reported in ``sweep``.  A step is one call of
 the op.  Inputs are synthetic and seeded, with the benchmark's distributions.
 
-For N > 1 GPUs (torchrun, one rank per GPU) the weight is column-sharded and
-the output all-gathered over NCCL: total work is fixed ("strong" scaling) and
-the time is the max over ranks.
+For N > 1 GPUs (torchrun, one rank per GPU) the weight is column-sharded:
+total work is fixed ("strong" scaling) and the time is the max over ranks.
+With ``--gather peer`` (the default) the GEMM epilogue stores every tile into
+all ranks' outputs over NVLink (one kernel per rank and call); with
+``--gather nccl`` the local output is all-gathered over NCCL and permuted.
 
 Timing: W untimed warm-up calls, then exactly K calls captured in a CUDA graph
 (N = 1) or launched eagerly (N > 1), bracketed by barrier + synchronize, timed
@@ -200,7 +202,10 @@ def run_ours(args, world, rank, device, peaks):
     n_local = N_DIM // world
     w_bytes = K_DIM * n_local // 2 + 2 * (K_DIM // GROUP) * n_local * 2
     sweep = {}
-    model = parallel.ColumnShardedW4A16(GROUP) if world > 1 else None
+    model = None
+    if world > 1:
+        model = (parallel.PeerGatherW4A16(GROUP) if args.gather == "peer"
+                 else parallel.ColumnShardedW4A16(GROUP))
     for M in sorted(set(args.sweep) | {args.m}):
         set_bytes = w_bytes + M * K_DIM * 2
         n_sets = max(2, min(8, -(-2 * L2_BYTES // set_bytes)))  # working set > 2x L2 where 8 sets allow
@@ -260,7 +265,7 @@ def run_ours(args, world, rank, device, peaks):
         e2e = {"value": round(e_ms * 1e3, 3), "unit": "us/call",
                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hx, hq, hs, hz)),
                "d2h_bytes_per_step": hy.numel() * hy.element_size(), "steps": e_steps,
-               "path": "ModelNew.forward" if world == 1 else "ColumnShardedW4A16.forward"}
+               "path": "ModelNew.forward" if world == 1 else f"{type(model).__name__}.forward"}
     return sweep, e2e, sampler.summary()
 
 
@@ -358,6 +363,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=HEADLINE_M)
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=list(SWEEP_M))
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-siblings", action="store_true")
@@ -427,10 +433,15 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
                 "data": "synthetic (seeded, benchmark distributions)",
                 "config": {"workload": workload,
-                           "parallelism": f"N-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                           "parallelism": (f"N-sharded x{world} + "
+                                           + ("all-gather fused in the GEMM epilogue (NVLink peer stores)"
+                                              if args.gather == "peer" else "NCCL all-gather")
+                                           if world > 1 else "single GPU"),
                            "l2": head["l2"]},
                 "roofline": roof, "sweep": {str(k): v for k, v in sweep.items()}, "siblings": siblings,
-                "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps}
+                "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+                # our kernels per step: the GEMM (with the gather fused into it for --gather peer)
+                "gpu_launches": args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

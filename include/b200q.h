@@ -129,6 +129,38 @@ int b200q_mxfp8_gemm(const void* a, const void* scales_a, const void* b, const v
 int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                              void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* stream);
 
+/* Column-sharded W4A16 GEMM with the all-gather fused into its epilogue.
+ * Computes columns [col0, col0 + N) of y = x . W from this rank's shard
+ * (qweight [K, N/8], scales/zeros [K/group, N]) and stores every finished
+ * tile into each of the n_peers buffers y_peers[i] ([M, ldy] row-major, the
+ * same dtype as x): normally y_peers[i] is rank i's full output mapped into
+ * this process (CUDA IPC / symmetric memory; NVLink peer stores, no
+ * multicast).  Needs col0 and ldy multiples of 32, col0 + N <= ldy,
+ * 1 <= n_peers <= 8; workspace as for b200q_w4a16_gemm with the shard's
+ * (M, N, K).
+ * pads: NULL, or rank i's signal pad for every i < n_peers (64 zeroed uint32
+ * words each, mapped into this process; this process's rank is `rank`).
+ * With pads the call orders itself against the peers, which must make the
+ * same sequence of calls: no rank stores into a peer's output before that
+ * peer has reached the same call, and the call completes on the stream only
+ * once every rank's columns have landed in every output.  A peer that does
+ * not arrive within 10 s sets B200Q_DEV_ERR_TIMEOUT in the status word.
+ * Without pads the ordering is the caller's (b200q_peer_barrier before and
+ * after).  No counterpart in the reference, which is single-GPU
+ * (generate_tasks.py:149); it replaces b200q_w4a16_gemm + an all-gather. */
+int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                           void* const* y_peers, int n_peers, int64_t ldy, int64_t col0, void* const* pads,
+                           int rank, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Barrier across the world ranks of one node, enqueued on `stream`.
+ * pads[i] is rank i's signal pad (as above; the barrier uses words disjoint
+ * from the GEMM's).  Orders this stream's earlier writes (peer stores
+ * included) before the peers' later work.  A rank that does not arrive within
+ * 10 s makes the wait give up and sets B200Q_DEV_ERR_TIMEOUT in the workspace
+ * status word. */
+int b200q_peer_barrier(void* const* pads, int world, int rank, void* workspace, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

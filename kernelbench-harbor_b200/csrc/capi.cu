@@ -3,20 +3,18 @@
 
 namespace b200q {
 size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
-int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
+int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);
 size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
-int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y, int64_t M,
-             int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
+             int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream);
 
 size_t w8a8_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
 int w8a8_tc(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y, int64_t M,
             int64_t N, int64_t K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
-// Rows from which the tensor-core (tcgen05) path is used.
-constexpr int64_t W4A16_TC_MIN_M = 33;
 
 static int check_w4a16_shape(int64_t M, int64_t N, int64_t K, int64_t group, int dtype) {
   if (dtype != B200Q_DTYPE_FP16 && dtype != B200Q_DTYPE_BF16)
@@ -51,8 +49,8 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16: null pointer argument");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (M >= W4A16_TC_MIN_M)
-    return w4a16_tc(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
-  return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, workspace, workspace_bytes, st);
+    return w4a16_tc(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
+  return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
 }
 
 size_t b200q_w8a8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device) {

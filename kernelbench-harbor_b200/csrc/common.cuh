@@ -31,6 +31,52 @@
 
 namespace b200q {
 
+// Output destinations of a GEMM: the same [M, N] tile is stored into every
+// y[i] at row stride ldy, column offset col0 (elements).  One destination with
+// ldy = N, col0 = 0 is a plain GEMM; the column-sharded multi-GPU GEMM passes
+// every rank's full [M, ldy] output (peer pointers over NVLink), so its
+// epilogue is also the all-gather.
+constexpr int MAX_PEERS = 8;
+
+// Rows from which the W4A16 tensor-core (tcgen05) path is used; fewer rows
+// take the mma.sync decode kernel.
+constexpr int64_t W4A16_TC_MIN_M = 33;
+//
+// With world > 1 the kernel also orders itself against the other ranks
+// through their signal pads (64 uint32 words per rank, zero-initialised,
+// every rank's mapped into each process), so that no separate barrier kernel
+// is needed:
+//   pad words [0, 8)   arrival epoch of call c from rank p (word p)
+//   pad words [8, 16)  completion epoch of call c from rank p (word 8 + p)
+//   pad word  62       ticket: CTAs of this rank's current call that finished
+//   pad word  63       calls this rank completed (its epoch counter)
+// At start one thread tells every peer "I am at call c+1" (this rank is done
+// reading its previous output); before its first peer store each CTA waits
+// until every peer is at call c+1; the last CTA to finish bumps the counter,
+// tells every peer "call c+1 complete" and waits for theirs.  All waits are
+// bounded.
+struct OutSet {
+  void* y[MAX_PEERS];
+  uint32_t* pad[MAX_PEERS];
+  int n;
+  int ldy;
+  int col0;
+  int world;  // 0 or 1: no cross-rank ordering
+  int rank;
+};
+
+constexpr int PAD_ARRIVE = 0, PAD_DONE = 8, PAD_BARRIER = 16, PAD_BARRIER_COUNT = 61, PAD_TICKET = 62,
+              PAD_COUNT = 63, PAD_WORDS = 64;
+
+inline OutSet single_out(void* y, int64_t N) {
+  OutSet o = {};
+  o.y[0] = y;
+  o.n = 1;
+  o.ldy = (int)N;
+  o.col0 = 0;
+  return o;
+}
+
 // ------------------------------------------------------------------ host side errors
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
@@ -56,6 +102,93 @@ __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+#ifndef B200Q_PEER_WAIT_NS
+#define B200Q_PEER_WAIT_NS 10000000000ull  // 10 s: ranks may legitimately arrive seconds apart
+#endif
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// Waits until (int)(*a - target) >= 0 (wrap-safe epochs); false after
+// B200Q_PEER_WAIT_NS.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* a, uint32_t target) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if ((int)(ld_acquire_sys(a) - target) >= 0) return true;
+    if ((it & 63) == 63 && globaltimer() - t0 > B200Q_PEER_WAIT_NS) return false;
+    __nanosleep(32);
+  }
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+// One thread: announce "at call c+1" to every peer.  Nothing this kernel
+// wrote needs ordering before it (the previous calls' reads of the output
+// ended with their kernels), so plain relaxed stores do: no fence.
+__device__ __forceinline__ void peer_arrive(const OutSet& o) {
+  if (o.world <= 1) return;
+  const uint32_t e = ld_volatile(o.pad[o.rank] + PAD_COUNT) + 1;
+  for (int p = 0; p < o.world; ++p)
+    if (p != o.rank) st_relaxed_sys(o.pad[p] + PAD_ARRIVE + o.rank, e);
+}
+
+// One thread, before the CTA's first store into a peer's output: every peer
+// is at call c+1.  Sets the timeout bit in *status and returns false on timeout.
+__device__ __forceinline__ bool peer_wait_arrivals(const OutSet& o, int* status) {
+  if (o.world <= 1) return true;
+  const uint32_t e = ld_volatile(o.pad[o.rank] + PAD_COUNT) + 1;
+  for (int p = 0; p < o.world; ++p)
+    if (p != o.rank && !wait_epoch(o.pad[o.rank] + PAD_ARRIVE + p, e)) {
+      atomicOr(status, B200Q_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  return true;
+}
+
+// Warp 0 of every CTA, after all of the CTA's stores (behind a CTA barrier).
+// Each CTA releases its stores at GPU scope into the ticket; the last CTA of
+// the grid (whose acquire of the ticket makes every CTA's stores precede it)
+// publishes "call c+1 complete" to every peer with a system-scope release,
+// one lane per peer, and waits for the peers' completions.
+__device__ __forceinline__ void peer_finish(const OutSet& o, int* status) {
+  if (o.world <= 1) return;
+  const int lane = threadIdx.x & 31;
+  uint32_t last = 0, e = 0;
+  if (lane == 0) {
+    const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+    uint32_t t;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(o.pad[o.rank] + PAD_TICKET) : "memory");
+    if (t == total - 1) {
+      last = 1;
+      o.pad[o.rank][PAD_TICKET] = 0;
+      e = ld_volatile(o.pad[o.rank] + PAD_COUNT) + 1;
+      o.pad[o.rank][PAD_COUNT] = e;
+    }
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  e = __shfl_sync(0xffffffffu, e, 0);
+  if (lane < o.world && lane != o.rank) {
+    st_release_sys(o.pad[lane] + PAD_DONE + o.rank, e);
+    if (!wait_epoch(o.pad[o.rank] + PAD_DONE + lane, e)) atomicOr(status, B200Q_DEV_ERR_TIMEOUT);
+  }
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -120,7 +120,7 @@ template <int MT, bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-                        void* __restrict__ y_, int M, int N, int K, int group, int strips, int splits,
+                        const __grid_constant__ OutSet out, int M, int N, int K, int group, int strips, int splits,
                         int n_stages_total, uint8_t* __restrict__ ws) {
   using L = Layout<MT>;
   using T = typename DT<BF16>::T;
@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     fence_barrier_init();
     s_err = 0;
+    if (blockIdx.x == 0 && blockIdx.y == 0) peer_arrive(out);
   }
   if (warp == NCONS && lane == 0) {
     prefetch_tmap(&tm_qw);
@@ -296,99 +297,117 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   __syncthreads();
-  if (s_err) return;  // status word already records the timeout
+  do {
+    if (s_err) break;  // status word already records the timeout
 
-  // ---------------------------------------------------------------- CTA reduction over the 4 K-quarters
-  float* red = reinterpret_cast<float*>(smem);
-  if (warp < NCONS) {
+    // ---------------------------------------------------------------- CTA reduction over the 4 K-quarters
+    float* red = reinterpret_cast<float*>(smem);
+    if (warp < NCONS) {
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int ti = 0; ti < 16; ++ti)
+        for (int ti = 0; ti < 16; ++ti)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) red[((warp * MT + mt) * 64 + ti * 4 + r) * 32 + lane] = acc[mt][ti][r];
-  }
-  __syncthreads();
-
-  // The CTA's output block is walked in fragment order: internal index
-  // i = ((nh * MT + mt) * 64 + e) * 32 + lane, e = tile * 4 + reg, which makes
-  // the smem reads above lane-contiguous (conflict-free).  Workspace slots use
-  // the same order; only the final store maps i to (row, column).
-  const int rows_here = min(16 * MT, M - mchunk * 16 * MT);
-  T* y = reinterpret_cast<T*>(y_);
-  const int n_int = 2 * MT * 64 * 32;
-  const size_t slot_elems = (size_t)n_int;
-  const size_t strip_id = (size_t)mchunk * strips + strip;
-  float* my_slot = partials + (strip_id * splits + split) * slot_elems;
-  const int tid = threadIdx.x;
-  auto row_of = [](int i) {  // row within the CTA block (0 .. 16*MT-1)
-    const int ln = i & 31, e = (i >> 5) & 63;
-    const int mt = (i >> 11) % MT;
-    return mt * 16 + (ln >> 2) + ((e & 3) >> 1) * 8;
-  };
-  auto col_of = [](int i) {  // column within the 256-column strip
-    const int ln = i & 31, e = (i >> 5) & 63, nh = (i >> 11) / MT;
-    const int tile = e >> 2, r = e & 3, om = tile >> 3, t = tile & 7, c = ln & 3;
-    return 8 * (nh * 16 + 2 * (2 * c + (r & 1)) + om) + t;
-  };
-  for (int i = tid; i < n_int; i += THREADS) {
-    const int row = row_of(i);
-    if (row >= rows_here) continue;
-    const int nh = (i >> 11) / MT, rest = i - nh * MT * 2048;
-    float v = 0.f;
-#pragma unroll
-    for (int kq = 0; kq < 4; ++kq) v += red[(kq * 2 + nh) * MT * 2048 + rest];
-    if (splits == 1) {
-      const int gcol = strip * STRIP_COLS + col_of(i);
-      if (gcol < N) y[(size_t)(mchunk * 16 * MT + row) * N + gcol] = (T)v;
-    } else {
-      my_slot[i] = v;
+          for (int r = 0; r < 4; ++r) red[((warp * MT + mt) * 64 + ti * 4 + r) * 32 + lane] = acc[mt][ti][r];
     }
-  }
-  if (splits == 1) return;
+    __syncthreads();
 
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(&tickets[strip_id], 1) == splits - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // all split slots of a float4 are loaded before any is summed (up to
-  // MAX_SPLITS independent L2 reads in flight per thread), then added in slot
-  // order, so the result does not depend on which CTA finished last.  The
-  // slots are cleared after reading: every workspace byte this kernel wrote
-  // goes back to zero (kernels sharing the workspace rely on zeroed memory).
-  float4* slots = reinterpret_cast<float4*>(partials + strip_id * splits * slot_elems);
-  const int slot4 = n_int / 4;
-  for (int i4 = tid; i4 < slot4; i4 += THREADS) {
-    const int i = i4 * 4;
-    const int row = row_of(i);  // the 4 lanes of a float4 share a row
-    if (row >= rows_here) continue;
-    float4 part[MAX_SPLITS];
+    // The CTA's output block is walked in fragment order: internal index
+    // i = ((nh * MT + mt) * 64 + e) * 32 + lane, e = tile * 4 + reg, which makes
+    // the smem reads above lane-contiguous (conflict-free).  Workspace slots use
+    // the same order; only the final store maps i to (row, column).
+    const int rows_here = min(16 * MT, M - mchunk * 16 * MT);
+    const int n_int = 2 * MT * 64 * 32;
+    const size_t slot_elems = (size_t)n_int;
+    const size_t strip_id = (size_t)mchunk * strips + strip;
+    float* my_slot = partials + (strip_id * splits + split) * slot_elems;
+    const int tid = threadIdx.x;
+    auto row_of = [](int i) {  // row within the CTA block (0 .. 16*MT-1)
+      const int ln = i & 31, e = (i >> 5) & 63;
+      const int mt = (i >> 11) % MT;
+      return mt * 16 + (ln >> 2) + ((e & 3) >> 1) * 8;
+    };
+    auto col_of = [](int i) {  // column within the 256-column strip
+      const int ln = i & 31, e = (i >> 5) & 63, nh = (i >> 11) / MT;
+      const int tile = e >> 2, r = e & 3, om = tile >> 3, t = tile & 7, c = ln & 3;
+      return 8 * (nh * 16 + 2 * (2 * c + (r & 1)) + om) + t;
+    };
+    if (splits == 1 && out.world > 1) {
+      if (tid == 0 && !peer_wait_arrivals(out, status)) s_err = 1;
+      __syncthreads();
+      if (s_err) break;
+    }
+    for (int i = tid; i < n_int; i += THREADS) {
+      const int row = row_of(i);
+      if (row >= rows_here) continue;
+      const int nh = (i >> 11) / MT, rest = i - nh * MT * 2048;
+      float v = 0.f;
 #pragma unroll
-    for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < splits) part[sp] = __ldcg(slots + sp * slot4 + i4);
-#pragma unroll
-    for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < splits) __stcg(slots + sp * slot4 + i4, make_float4(0.f, 0.f, 0.f, 0.f));
-    float4 v = part[0];
-#pragma unroll
-    for (int sp = 1; sp < MAX_SPLITS; ++sp)
-      if (sp < splits) {
-        v.x += part[sp].x;
-        v.y += part[sp].y;
-        v.z += part[sp].z;
-        v.w += part[sp].w;
+      for (int kq = 0; kq < 4; ++kq) v += red[(kq * 2 + nh) * MT * 2048 + rest];
+      if (splits == 1) {
+        const int gcol = strip * STRIP_COLS + col_of(i);
+        if (gcol < N)
+          for (int o = 0; o < out.n; ++o)
+            reinterpret_cast<T*>(out.y[o])[(size_t)(mchunk * 16 * MT + row) * out.ldy + out.col0 + gcol] = (T)v;
+      } else {
+        my_slot[i] = v;
       }
-    T* yr = y + (size_t)(mchunk * 16 * MT + row) * N + strip * STRIP_COLS;
-    const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int col = col_of(i + q);
-      if (strip * STRIP_COLS + col < N) yr[col] = (T)vv[q];
     }
+    if (splits == 1) break;
+
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&tickets[strip_id], 1) == splits - 1);
+    __syncthreads();
+    if (!s_last) break;
+    __threadfence();
+    if (out.world > 1) {
+      if (tid == 0 && !peer_wait_arrivals(out, status)) s_err = 1;
+      __syncthreads();
+      if (s_err) break;
+    }
+    // all split slots of a float4 are loaded before any is summed (up to
+    // MAX_SPLITS independent L2 reads in flight per thread), then added in slot
+    // order, so the result does not depend on which CTA finished last.  The
+    // slots are cleared after reading: every workspace byte this kernel wrote
+    // goes back to zero (kernels sharing the workspace rely on zeroed memory).
+    float4* slots = reinterpret_cast<float4*>(partials + strip_id * splits * slot_elems);
+    const int slot4 = n_int / 4;
+    for (int i4 = tid; i4 < slot4; i4 += THREADS) {
+      const int i = i4 * 4;
+      const int row = row_of(i);  // the 4 lanes of a float4 share a row
+      if (row >= rows_here) continue;
+      float4 part[MAX_SPLITS];
+#pragma unroll
+      for (int sp = 0; sp < MAX_SPLITS; ++sp)
+        if (sp < splits) part[sp] = __ldcg(slots + sp * slot4 + i4);
+#pragma unroll
+      for (int sp = 0; sp < MAX_SPLITS; ++sp)
+        if (sp < splits) __stcg(slots + sp * slot4 + i4, make_float4(0.f, 0.f, 0.f, 0.f));
+      float4 v = part[0];
+#pragma unroll
+      for (int sp = 1; sp < MAX_SPLITS; ++sp)
+        if (sp < splits) {
+          v.x += part[sp].x;
+          v.y += part[sp].y;
+          v.z += part[sp].z;
+          v.w += part[sp].w;
+        }
+      const size_t yoff = (size_t)(mchunk * 16 * MT + row) * out.ldy + out.col0 + strip * STRIP_COLS;
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int col = col_of(i + q);
+        if (strip * STRIP_COLS + col < N)
+          for (int o = 0; o < out.n; ++o) reinterpret_cast<T*>(out.y[o])[yoff + col] = (T)vv[q];
+      }
+    }
+    if (tid == 0) tickets[strip_id] = 0;  // leave the workspace zeroed for the next call
+  } while (0);
+  if (out.world > 1) {
+    __syncthreads();
+    if (threadIdx.x < 32) peer_finish(out, status);
   }
-  if (tid == 0) tickets[strip_id] = 0;  // leave the workspace zeroed for the next call
 }
 
 struct Plan {
@@ -417,7 +436,7 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
 
 template <int MT, bool BF16>
 static int launch_t(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s,
-                    const CUtensorMap& z, void* y, int M, int N, int K, int group, uint8_t* ws,
+                    const CUtensorMap& z, const OutSet& y, int M, int N, int K, int group, uint8_t* ws,
                     cudaStream_t stream) {
   auto kern = w4a16_decode_kernel<MT, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<MT>::SMEM);
@@ -434,7 +453,7 @@ size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
   return decode::plan(M, N, K, num_sms(device)).ws_bytes;
 }
 
-int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
+int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream) {
   using namespace decode;

@@ -28,7 +28,7 @@
 
 namespace b200q {
 size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
-int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y,
+int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);
 }  // namespace b200q
@@ -90,5 +90,5 @@ extern "C" int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, c
   const size_t tickets = ((size_t)2 * ((N + 255) / 256) * 4 + 255) & ~size_t(255);
   const size_t clear = need < 256 + tickets ? need : 256 + tickets;
   if ((rc = check_cuda(cudaMemsetAsync(scratch, 0, clear, st), "noalloc scratch clear"))) return rc;
-  return w4a16_decode(x, qweight, scales, zeros, y, M, N, K, group, dtype, scratch, NOALLOC_SCRATCH_BYTES, st);
+  return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, scratch, NOALLOC_SCRATCH_BYTES, st);
 }

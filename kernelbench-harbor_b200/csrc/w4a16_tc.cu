@@ -165,7 +165,7 @@ template <bool BF16, int MB>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wq,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-                    void* __restrict__ y_, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws) {
+                    const __grid_constant__ OutSet out, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws) {
   using T = typename DT<BF16>::T;
   using C = Cfg<MB>;
   constexpr int SX = C::SX, SW = C::SW, S2 = C::S2;
@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_s);
     prefetch_tmap(&tm_z);
   }
+  if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) peer_arrive(out);
   if (warp == W_MMA) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -324,15 +325,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 
     // ---------------------------------------------------------------- epilogue: TMEM -> y
-    if (!s_err && mbar_wait(acc_full, 0, status)) {
+    const bool acc_ok = !s_err && mbar_wait(acc_full, 0, status);
+    if (!acc_ok) s_err = 1;
+    if (acc_ok) {
       tc_fence_after();
       const int qd = warp & 3;   // TMEM lane quadrant this warp may access
       const int part = dw >> 2;  // which of the NDQ/4 column ranges of this quadrant
       constexpr int COLS = MB * BN / (NDQ / 4);  // lies within one accumulator
       const int acc = (part * COLS) / BN;
       const int trow = acc * BM + qd * 32 + lane;  // row within the CTA tile
-      const int row = m0 + trow;
-      T* y = reinterpret_cast<T*>(y_);
 #pragma unroll 1
       for (int c0 = 0; c0 < COLS; c0 += 32) {
         const int tcol = part * COLS + c0;  // TMEM column: accumulator acc, column tcol % BN
@@ -344,21 +345,45 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int p = 0; p < 32; ++p) v[(p & ~7) | slot_col(p & 7)] = __uint_as_float(r[p]);
         if (splits == 1) {
-          const int col = n0 + cslot;
-          if (row < M && col < N) {
-            uint32_t packed[16];
+          // stage the tile in shared memory (the operand rings are idle once
+          // the accumulator is complete): row trow is 512 bytes of 32 16-byte
+          // chunks, chunk index XOR-swizzled by the row so that both the
+          // row-per-lane writes here and the chunk-per-lane reads below are
+          // free of bank conflicts
+          uint32_t packed[16];
 #pragma unroll
-            for (int p = 0; p < 16; ++p) {
-              if (!BF16)
-                packed[p] = as_u32(__floats2half2_rn(v[2 * p], v[2 * p + 1]));
-              else
-                packed[p] = as_u32(__floats2bfloat162_rn(v[2 * p], v[2 * p + 1]));
-            }
-            uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * N + col);
-#pragma unroll
-            for (int p = 0; p < 4; ++p)
-              dst[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+          for (int p = 0; p < 16; ++p) {
+            if (!BF16)
+              packed[p] = as_u32(__floats2half2_rn(v[2 * p], v[2 * p + 1]));
+            else
+              packed[p] = as_u32(__floats2bfloat162_rn(v[2 * p], v[2 * p + 1]));
           }
+          uint8_t* srow = smem + (uint32_t)trow * (BN * 2);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int chunk = (cslot >> 3) + p;
+            *reinterpret_cast<uint4*>(srow + ((chunk ^ (trow & 31)) << 4)) =
+                make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+          }
+        }
+      }
+    }
+    if (splits == 1) {
+      // every row leaves as whole 512-byte lines, one per warp instruction
+      // and destination: coalesced in HBM and few, large NVLink writes
+      if (warp == W_DQ0 && lane == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
+      named_barrier_sync(1, NDQ * 32);  // all epilogue warps, failed or not
+      if (!s_err) {
+        const int col = n0 + lane * 8;
+#pragma unroll 1
+        for (int r = dw; r < MB * BM; r += NDQ) {
+          const int grow = m0 + r;
+          if (grow >= M) break;
+          const uint4 val = *reinterpret_cast<const uint4*>(smem + (uint32_t)r * (BN * 2) + ((lane ^ (r & 31)) << 4));
+          if (col < N)
+            for (int o = 0; o < out.n; ++o)
+              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(out.y[o]) + (size_t)grow * out.ldy + out.col0 + col) =
+                  val;
         }
       }
     }
@@ -398,10 +423,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           st_cluster_v4(base + (cslot + 4 * p) * 4, v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
       }
     }
+    if (threadIdx.x == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
     cluster_sync();
     if (!s_err) {
       const float* buf = reinterpret_cast<const float*>(smem);
-      T* y = reinterpret_cast<T*>(y_);
       for (int e = threadIdx.x * 4; e < (int)(R * BN); e += THREADS * 4) {
         const int lr = e / BN, c = e % BN;
         float4 acc4 = reinterpret_cast<const float4*>(buf + lr * BN + c)[0];
@@ -414,11 +439,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const int row = m0 + (int)(rank * R) + lr, col = n0 + c;
         if (row < M && col < N) {
-          T* d = y + (size_t)row * N + col;
-          d[0] = (T)acc4.x;
-          d[1] = (T)acc4.y;
-          d[2] = (T)acc4.z;
-          d[3] = (T)acc4.w;
+          uint2 packed;
+          if (!BF16) {
+            packed.x = as_u32(__floats2half2_rn(acc4.x, acc4.y));
+            packed.y = as_u32(__floats2half2_rn(acc4.z, acc4.w));
+          } else {
+            packed.x = as_u32(__floats2bfloat162_rn(acc4.x, acc4.y));
+            packed.y = as_u32(__floats2bfloat162_rn(acc4.z, acc4.w));
+          }
+          for (int o = 0; o < out.n; ++o)
+            *reinterpret_cast<uint2*>(reinterpret_cast<T*>(out.y[o]) + (size_t)row * out.ldy + out.col0 + col) =
+                packed;
         }
       }
     }
@@ -426,6 +457,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (out.world > 1) {
+    __syncthreads();
+    if (threadIdx.x < 32) peer_finish(out, status);
   }
 }
 
@@ -464,8 +499,8 @@ size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
   return tc::plan(M, N, K, num_sms(device)).ws_bytes;
 }
 
-int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, void* y, int64_t M,
-             int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& out,
+             int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream) {
   using namespace tc;
   Plan p = plan(M, N, K, num_sms(-1));
@@ -521,7 +556,7 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
   attr[0].val.clusterDim.z = (unsigned)p.splits;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, tx, twq, ts, tz, y, (int)M, (int)N, (int)K, (int)group, p.splits,
+  e = cudaLaunchKernelEx(&cfg, kern, tx, twq, ts, tz, out, (int)M, (int)N, (int)K, (int)group, p.splits,
                          reinterpret_cast<uint8_t*>(workspace));
   if (e != cudaSuccess) return check_cuda(e, "w4a16 tc launch");
   return check_cuda(cudaGetLastError(), "w4a16 tc launch");

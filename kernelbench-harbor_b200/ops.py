@@ -96,6 +96,48 @@ def _(x, qweight, scales, zeros, group):
     return x.new_empty((x.shape[0], qweight.shape[1] * 8))
 
 
+def _ptr_array(ptrs) -> "ctypes.Array":
+    import ctypes
+    return (ctypes.c_void_p * len(ptrs))(*[int(p) for p in ptrs])
+
+
+def w4a16_gemm_peers(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+                     group: int, y_ptrs, ldy: int, col0: int, pad_ptrs=None, rank: int = 0) -> None:
+    """Columns [col0, col0 + N) of y = x . W from this rank's shard, stored
+    into every buffer of ``y_ptrs`` (device addresses of [M, ldy] arrays in
+    x.dtype, peers' included).  With ``pad_ptrs`` (every rank's signal pad)
+    the kernel orders itself against the peers; without, the caller does
+    (``peer_barrier`` before and after)."""
+    if not x.is_cuda:
+        raise RuntimeError("w4a16_gemm_peers runs on CUDA tensors only (no CPU implementation)")
+    M, K = x.shape
+    N = qweight.shape[1] * 8
+    if qweight.dtype != torch.int32 or qweight.shape[0] != K:
+        raise ValueError("qweight must be int32 [K, N/8]")
+    dt = _dtype_code(x.dtype)
+    scales = scales.to(x.dtype)
+    zeros = zeros.to(x.dtype)
+    x, qweight, scales, zeros = (_aligned(t) for t in (x, qweight, scales, zeros))
+    if M == 0:
+        return
+    L = _lib.lib()
+    ws = workspace(x.device, L.b200q_w4a16_workspace_bytes(M, N, K, group, x.device.index))
+    arr = _ptr_array(y_ptrs)
+    pads = _ptr_array(pad_ptrs) if pad_ptrs is not None else None
+    _lib.check(L.b200q_w4a16_gemm_peers(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                                        arr, len(y_ptrs), ldy, col0, pads, rank, M, N, K, group, dt,
+                                        ws.data_ptr(), ws.numel(), _stream_ptr(x.device)))
+
+
+def peer_barrier(pad_ptrs, rank: int, device: torch.device) -> None:
+    """Barrier of the len(pad_ptrs) ranks on the current stream (signal pads
+    of 64 zeroed uint32 words, every rank's mapped into this process)."""
+    L = _lib.lib()
+    ws = workspace(device, 256)
+    _lib.check(L.b200q_peer_barrier(_ptr_array(pad_ptrs), len(pad_ptrs), rank, ws.data_ptr(),
+                                    _stream_ptr(device)))
+
+
 @torch.library.custom_op("b200q::w8a8_gemm", mutates_args=())
 def w8a8_gemm(x_int8: torch.Tensor, w_int8: torch.Tensor, x_scale: torch.Tensor,
               w_scale: torch.Tensor) -> torch.Tensor:

@@ -8,6 +8,15 @@ replicated.  The one exchange step is an all-gather of the [M, N/P] output
 slices over NCCL (NVLink/NVSwitch), gathered as [P, M, N/P] and laid out as
 [M, N].  Nothing else is partitioned.
 
+Two forms of the exchange:
+  * ``ColumnShardedW4A16``: local GEMM into [M, N/P], then an NCCL
+    all-gather and a column permute (the plain tensor-parallel baseline);
+  * ``PeerGatherW4A16``: the GEMM epilogue itself stores every finished tile
+    into all ranks' [M, N] outputs over NVLink (peer-mapped symmetric memory,
+    plain stores) and orders itself against the peers through signal pads,
+    so the whole sharded call is one kernel launch per rank: the exchange
+    overlaps the tiles still being computed and no gather or permute follows.
+
 The reference has no multi-GPU path (every task is gpus = 1,
 generate_tasks.py:149); this module is the benchmark's sharded configuration.
 """
@@ -72,6 +81,81 @@ class ColumnShardedW4A16(nn.Module):
         if world == 1:
             return y_local
         return gather_columns(y_local, world, self.pg)
+
+
+class PeerBuffers:
+    """Per-process cache of peer-mapped ("symmetric") CUDA buffers: an output
+    buffer of at least the requested bytes and a zeroed signal pad, each
+    rendezvoused with every rank of the group so that this process holds
+    device addresses of all ranks' copies.  Allocation is collective: every
+    rank must request the same sizes in the same order (true of a
+    column-sharded layer, whose M and N agree across ranks).  NVLink multicast
+    objects are not created (TORCH_SYMM_MEM_DISABLE_MULTICAST=1): the kernels
+    use plain peer stores only."""
+
+    PAD_WORDS = 64
+
+    def __init__(self, device: torch.device, process_group: Optional[dist.ProcessGroup] = None):
+        import os
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        self._symm = symm_mem
+        self.device = device
+        self.pg = process_group or dist.group.WORLD
+        self.rank = dist.get_rank(self.pg)
+        self.world = dist.get_world_size(self.pg)
+        self._out = None
+        self._out_handle = None
+        pad = symm_mem.empty(self.PAD_WORDS, dtype=torch.int32, device=device)
+        pad.zero_()
+        self._pad = pad
+        self._pad_handle = symm_mem.rendezvous(pad, self.pg)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.pg)
+        self.pad_ptrs = list(self._pad_handle.buffer_ptrs)
+
+    def output(self, nbytes: int):
+        """(local uint8 tensor of >= nbytes, every rank's address of it)."""
+        if self._out is None or self._out.numel() < nbytes:
+            torch.cuda.synchronize(self.device)  # no peer store into the old buffer is in flight
+            dist.barrier(group=self.pg)
+            self._out = None
+            self._out_handle = None
+            buf = self._symm.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=self.device)
+            self._out_handle = self._symm.rendezvous(buf, self.pg)
+            self._out = buf
+        return self._out, list(self._out_handle.buffer_ptrs)
+
+
+class PeerGatherW4A16(nn.Module):
+    """Tensor-parallel W4A16 linear whose all-gather is fused into the GEMM:
+    one kernel per rank stores this rank's columns into every rank's y over
+    NVLink, waiting before its first store until every peer has reached the
+    same call (so no peer still reads its previous output) and completing only
+    once all columns have landed.  Returns y [M, N] in x.dtype, a view of this
+    module's peer-mapped buffer: it stays valid until the next forward call."""
+
+    def __init__(self, group_size: int = 128, process_group: Optional[dist.ProcessGroup] = None):
+        super().__init__()
+        self.group_size = group_size
+        self.pg = process_group
+        self._bufs: Optional[PeerBuffers] = None
+
+    def forward(self, x: torch.Tensor, qweight_shard: torch.Tensor, scales_shard: torch.Tensor,
+                zeros_shard: torch.Tensor) -> torch.Tensor:
+        from . import ops
+        world = dist.get_world_size(self.pg)
+        rank = dist.get_rank(self.pg)
+        M = x.shape[0]
+        n = qweight_shard.shape[1] * 8
+        N = n * world
+        if self._bufs is None:
+            self._bufs = PeerBuffers(x.device, self.pg)
+        buf, ptrs = self._bufs.output(M * N * x.element_size())
+        y = buf[:M * N * x.element_size()].view(x.dtype).view(M, N)
+        ops.w4a16_gemm_peers(x, qweight_shard, scales_shard, zeros_shard, self.group_size, ptrs, N, rank * n,
+                             self._bufs.pad_ptrs, rank)
+        return y
 
 
 class ExpertParallelMoE(nn.Module):
