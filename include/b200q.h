@@ -129,6 +129,24 @@ int b200q_mxfp8_gemm(const void* a, const void* scales_a, const void* b, const v
 int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                              void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* stream);
 
+/* Grouped W4A16 GEMM over the experts of a MoE layer, one launch for all
+ * experts.  x [rows, K] holds every expert's rows contiguously, expert e's at
+ * [offsets[e], offsets[e+1]) (offsets [E+1] int32 on the device, as written
+ * by b200q_moe_route; read by the kernel, so no host synchronisation).
+ * Expert weights are stacked: qweight [E, K, N/8] int32, scales / zeros
+ * [E, K/group, N] in x's dtype.  Without the *_up arrays (NULL):
+ * y [rows, N] = x . W_e row by row.  With them (the gate and up projections,
+ * same shapes): y [rows, N] = SiLU(x . Wg_e) * (x . Wu_e), the products
+ * rounded to the activation type before SiLU and the result rounded once, as
+ * b200q_w4a16_gemm + b200q_silu_mul compute it.  K a multiple of 64,
+ * 1 <= E <= 64, workspace >= 256 bytes (status word).  Replaces the
+ * per-expert loop of FUSED_QMOE_REF.forward (generate_tasks.py:372-378) and
+ * the SiLU.mul of FUSED_SILU_REF (:336-337). */
+int b200q_moe_grouped_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                           const int32_t* qweight_up, const void* scales_up, const void* zeros_up,
+                           const int32_t* offsets, int64_t E, void* y, int64_t rows, int64_t N, int64_t K,
+                           int64_t group, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Column-sharded W4A16 GEMM with the all-gather fused into its epilogue.
  * Computes columns [col0, col0 + N) of y = x . W from this rank's shard
  * (qweight [K, N/8], scales/zeros [K/group, N]) and stores every finished

@@ -49,6 +49,9 @@ SIGNATURES = {
     "b200q_w4a16_gemm_peers": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, ctypes.c_int, _c_i64, _c_i64,
                                               _c_vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
                                               _c_vp, _c_sz, _c_vp]),
+    "b200q_moe_grouped_gemm": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64,
+                                              _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_sz,
+                                              _c_vp]),
     "b200q_peer_barrier": (ctypes.c_int, [_c_vp, ctypes.c_int, ctypes.c_int, _c_vp, _c_vp]),
 }
 

@@ -11,6 +11,11 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
              int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream);
 
+int w4a16_tc_grouped(const void* x, const int32_t* qw, const void* sc, const void* zr, const int32_t* qw2,
+                     const void* sc2, const void* zr2, const int32_t* offsets, int64_t E, void* y, int64_t rows,
+                     int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream);
+
 size_t w8a8_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
 int w8a8_tc(const void* x_int8, const void* w_int8, const void* x_scale, const void* w_scale, void* y, int64_t M,
             int64_t N, int64_t K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
@@ -51,6 +56,26 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (M >= W4A16_TC_MIN_M)
     return w4a16_tc(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
   return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
+}
+
+int b200q_moe_grouped_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                           const int32_t* qweight_up, const void* scales_up, const void* zeros_up,
+                           const int32_t* offsets, int64_t E, void* y, int64_t rows, int64_t N, int64_t K,
+                           int64_t group, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace b200q;
+  int rc = check_w4a16_shape(rows, N, K, group, dtype);
+  if (rc) return rc;
+  if (E < 1 || E > 64) return fail(B200Q_ERR_SHAPE, "moe_grouped_gemm: need 1 <= E <= 64");
+  if (K % 64) return fail(B200Q_ERR_ALIGN, "moe_grouped_gemm: K must be a multiple of 64");
+  if (E * K > (1ll << 31) - 1) return fail(B200Q_ERR_SHAPE, "moe_grouped_gemm: E*K too large");
+  const bool glu = qweight_up || scales_up || zeros_up;
+  if (glu && !(qweight_up && scales_up && zeros_up))
+    return fail(B200Q_ERR_SHAPE, "moe_grouped_gemm: give all three up-projection arrays or none");
+  if (rows == 0) return B200Q_OK;
+  if (!x || !qweight || !scales || !zeros || !offsets || !y)
+    return fail(B200Q_ERR_SHAPE, "moe_grouped_gemm: null pointer argument");
+  return w4a16_tc_grouped(x, qweight, scales, zeros, qweight_up, scales_up, zeros_up, offsets, E, y, rows, N, K,
+                          group, dtype, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t b200q_w8a8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device) {

@@ -161,11 +161,30 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, const ColQ& q) {
 // B-operand slot -> actual column within each group of 8
 __device__ __forceinline__ int slot_col(int p) { return ((p & 1) << 2) | (p >> 1); }
 
-template <bool BF16, int MB>
+// Grouped (per-expert) operation: blockIdx.y enumerates the 128-row tiles of
+// every expert's contiguous row block [offsets[e], offsets[e+1]) of x (the
+// routing kernel's grouping), expert e's weights are rows [e*K, (e+1)*K) of
+// the stacked qweight (scales / zeros rows [e*K/g, (e+1)*K/g)).  With GLU the
+// tile's 256 B-columns are 128 columns of the gate weight (tm_wq / tm_s /
+// tm_z) and the same 128 columns of the up weight (wq2 / s2 / z2), and the
+// epilogue writes h = SiLU(x.Wg) * (x.Wu) for those 128 columns.
+struct Grouped {
+  CUtensorMap wq2, s2, z2;
+  const int32_t* offsets;
+  int E;
+};
+
+enum { MODE_PLAIN = 0, MODE_GROUPED = 1, MODE_GLU = 2 };
+
+template <bool BF16, int MB, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wq,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-                    const __grid_constant__ OutSet out, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws) {
+                    const __grid_constant__ OutSet out, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws,
+                    const __grid_constant__ Grouped grp) {
+  static_assert(MODE == MODE_PLAIN || MB == 1, "grouped tiles are 128 rows");
+  constexpr bool GLU = MODE == MODE_GLU;
+  constexpr int OUTC = GLU ? BN / 2 : BN;  // output columns per tile
   using T = typename DT<BF16>::T;
   using C = Cfg<MB>;
   constexpr int SX = C::SX, SW = C::SW, S2 = C::S2;
@@ -186,7 +205,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   int* status = reinterpret_cast<int*>(ws);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
-  const int n0 = n_tile * BN, m0 = m_tile * BM * MB;
+  const int n0 = n_tile * OUTC;  // first output (and weight) column of the tile
+  int m0 = m_tile * BM * MB, m_end = M, wk0 = 0;
+  if (MODE != MODE_PLAIN) {
+    // find this CTA's expert and row tile; CTAs past the last tile exit
+    int e = 0, t = m_tile;
+    for (; e < grp.E; ++e) {
+      const int a = grp.offsets[e], b = grp.offsets[e + 1];
+      const int tiles = (b - a + BM - 1) / BM;
+      if (t < tiles) {
+        m0 = a + t * BM;
+        m_end = b;
+        break;
+      }
+      t -= tiles;
+    }
+    if (e == grp.E) return;
+    wk0 = e * K;
+  }
   const int nk_total = (K + BK - 1) / BK;
   const int k_begin = (int)((long long)split * nk_total / splits);
   const int k_end = (int)((long long)(split + 1) * nk_total / splits);
@@ -233,11 +269,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           s_err = 1;
           break;
         }
-        const int kb = (k_begin + it) * BK;
+        const int kb = wk0 + (k_begin + it) * BK;
         mbar_arrive_expect_tx(&w_full[s], stage_tx);
-        tma_load_2d(smem + OFF_WQ + s * WQ_BYTES, &tm_wq, n0 / 8, kb, &w_full[s]);
-        tma_load_2d(smem + OFF_S + s * SZ_BYTES, &tm_s, n0, kb / group, &w_full[s]);
-        tma_load_2d(smem + OFF_Z + s * SZ_BYTES, &tm_z, n0, kb / group, &w_full[s]);
+        if (!GLU) {
+          tma_load_2d(smem + OFF_WQ + s * WQ_BYTES, &tm_wq, n0 / 8, kb, &w_full[s]);
+          tma_load_2d(smem + OFF_S + s * SZ_BYTES, &tm_s, n0, kb / group, &w_full[s]);
+          tma_load_2d(smem + OFF_Z + s * SZ_BYTES, &tm_z, n0, kb / group, &w_full[s]);
+        } else {
+          // gate words then up words, [BK][16] each; scale / zero rows as
+          // 128 gate columns then 128 up columns
+          tma_load_2d(smem + OFF_WQ + s * WQ_BYTES, &tm_wq, n0 / 8, kb, &w_full[s]);
+          tma_load_2d(smem + OFF_WQ + s * WQ_BYTES + WQ_BYTES / 2, &grp.wq2, n0 / 8, kb, &w_full[s]);
+          for (int r = 0; r < srows; ++r) {
+            uint8_t* srow = smem + OFF_S + s * SZ_BYTES + r * BN * 2;
+            uint8_t* zrow = smem + OFF_Z + s * SZ_BYTES + r * BN * 2;
+            tma_load_2d(srow, &tm_s, n0, kb / group + r, &w_full[s]);
+            tma_load_2d(srow + BN, &grp.s2, n0, kb / group + r, &w_full[s]);
+            tma_load_2d(zrow, &tm_z, n0, kb / group + r, &w_full[s]);
+            tma_load_2d(zrow + BN, &grp.z2, n0, kb / group + r, &w_full[s]);
+          }
+        }
       }
     }
   } else if (warp == W_XPROD) {
@@ -310,7 +361,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const ColQ q1 = srows > 1 ? load_colq<BF16>(srow0 + BN * 2, zrow0 + BN * 2, lane) : q0;
       uint32_t wv[WORDS];
 #pragma unroll
-      for (int i = 0; i < WORDS; ++i) wv[i] = wq[(rr + 8 * (WPR * i + (dw >> 3))) * 32 + lane];
+      for (int i = 0; i < WORDS; ++i) {
+        const int row = rr + 8 * (WPR * i + (dw >> 3));
+        wv[i] = GLU ? wq[(lane >> 4) * (BK * 16) + row * 16 + (lane & 15)] : wq[row * 32 + lane];
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[s]);
 #pragma unroll
@@ -325,31 +379,47 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 
     // ---------------------------------------------------------------- epilogue: TMEM -> y
+    // The tile is staged in shared memory (the operand rings are idle once the
+    // accumulator is complete) as rows of OUTC output values: CH 16-byte
+    // chunks per row, the chunk index XOR-swizzled by the row so that both the
+    // row-per-lane writes here and the chunk-per-lane reads below are free of
+    // bank conflicts.  Rows then leave as whole lines (512 B, or 256 B with
+    // GLU), coalesced in HBM and as few, large NVLink writes.
+    constexpr int CH = OUTC / 8;
     const bool acc_ok = !s_err && mbar_wait(acc_full, 0, status);
     if (!acc_ok) s_err = 1;
     if (acc_ok) {
       tc_fence_after();
       const int qd = warp & 3;   // TMEM lane quadrant this warp may access
       const int part = dw >> 2;  // which of the NDQ/4 column ranges of this quadrant
-      constexpr int COLS = MB * BN / (NDQ / 4);  // lies within one accumulator
-      const int acc = (part * COLS) / BN;
+      constexpr int COLS = MB * OUTC / (NDQ / 4);  // lies within one accumulator
+      const int acc = (part * COLS) / OUTC;
       const int trow = acc * BM + qd * 32 + lane;  // row within the CTA tile
+      const uint32_t tl = tmem + ((uint32_t)(qd * 32) << 16);
 #pragma unroll 1
       for (int c0 = 0; c0 < COLS; c0 += 32) {
-        const int tcol = part * COLS + c0;  // TMEM column: accumulator acc, column tcol % BN
-        const int cslot = tcol % BN;
+        const int tcol = part * COLS + c0;  // output column tcol % OUTC of accumulator acc
+        const int ocol = tcol % OUTC;
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + tcol, r);
-        tmem_ld_wait();
         float v[32];
+        tmem_ld32(tl + acc * BN + ocol, r);
+        tmem_ld_wait();
 #pragma unroll
         for (int p = 0; p < 32; ++p) v[(p & ~7) | slot_col(p & 7)] = __uint_as_float(r[p]);
+        if (GLU) {
+          // up columns sit 128 TMEM columns to the right; h = SiLU(g) * u with
+          // g and u rounded to the activation type first and one rounding of
+          // the product, as the unfused gate/up GEMMs + silu_mul compute it
+          tmem_ld32(tl + ocol + BN / 2, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int p = 0; p < 32; ++p) {
+            const float g = (float)(T)v[(p & ~7) | slot_col(p & 7)];
+            const float u = (float)(T)__uint_as_float(r[p]);
+            v[(p & ~7) | slot_col(p & 7)] = g / (1.f + expf(-g)) * u;
+          }
+        }
         if (splits == 1) {
-          // stage the tile in shared memory (the operand rings are idle once
-          // the accumulator is complete): row trow is 512 bytes of 32 16-byte
-          // chunks, chunk index XOR-swizzled by the row so that both the
-          // row-per-lane writes here and the chunk-per-lane reads below are
-          // free of bank conflicts
           uint32_t packed[16];
 #pragma unroll
           for (int p = 0; p < 16; ++p) {
@@ -358,28 +428,29 @@ __global__ void __launch_bounds__(THREADS, 1)
             else
               packed[p] = as_u32(__floats2bfloat162_rn(v[2 * p], v[2 * p + 1]));
           }
-          uint8_t* srow = smem + (uint32_t)trow * (BN * 2);
+          uint8_t* srow = smem + (uint32_t)trow * (OUTC * 2);
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
-            const int chunk = (cslot >> 3) + p;
-            *reinterpret_cast<uint4*>(srow + ((chunk ^ (trow & 31)) << 4)) =
+            const int chunk = (ocol >> 3) + p;
+            *reinterpret_cast<uint4*>(srow + ((chunk ^ (trow % CH)) << 4)) =
                 make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
           }
         }
       }
     }
     if (splits == 1) {
-      // every row leaves as whole 512-byte lines, one per warp instruction
-      // and destination: coalesced in HBM and few, large NVLink writes
       if (warp == W_DQ0 && lane == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
       named_barrier_sync(1, NDQ * 32);  // all epilogue warps, failed or not
       if (!s_err) {
-        const int col = n0 + lane * 8;
+        constexpr int RPW = 32 / CH;  // rows per warp instruction
+        const int chunk = lane % CH;
+        const int col = n0 + chunk * 8;
 #pragma unroll 1
-        for (int r = dw; r < MB * BM; r += NDQ) {
+        for (int r = dw * RPW + lane / CH; r < MB * BM; r += NDQ * RPW) {
           const int grow = m0 + r;
-          if (grow >= M) break;
-          const uint4 val = *reinterpret_cast<const uint4*>(smem + (uint32_t)r * (BN * 2) + ((lane ^ (r & 31)) << 4));
+          if (grow >= m_end) break;
+          const uint4 val =
+              *reinterpret_cast<const uint4*>(smem + (uint32_t)r * (OUTC * 2) + ((chunk ^ (r % CH)) << 4));
           if (col < N)
             for (int o = 0; o < out.n; ++o)
               *reinterpret_cast<uint4*>(reinterpret_cast<T*>(out.y[o]) + (size_t)grow * out.ldy + out.col0 + col) =
@@ -519,8 +590,8 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
   if ((rc = encode_2d(&tz, h16, zeros, N, K / group, (uint64_t)N * 2, BN, srows, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   const bool bf = dtype == B200Q_DTYPE_BF16;
-  auto kern = p.mb == 2 ? (bf ? w4a16_tc_kernel<true, 2> : w4a16_tc_kernel<false, 2>)
-                        : (bf ? w4a16_tc_kernel<true, 1> : w4a16_tc_kernel<false, 1>);
+  auto kern = p.mb == 2 ? (bf ? w4a16_tc_kernel<true, 2, MODE_PLAIN> : w4a16_tc_kernel<false, 2, MODE_PLAIN>)
+                        : (bf ? w4a16_tc_kernel<true, 1, MODE_PLAIN> : w4a16_tc_kernel<false, 1, MODE_PLAIN>);
   const uint32_t smem = p.mb == 2 ? Cfg<2>::SMEM : Cfg<1>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 tc)");
@@ -556,10 +627,61 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
   attr[0].val.clusterDim.z = (unsigned)p.splits;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  Grouped none = {};
   e = cudaLaunchKernelEx(&cfg, kern, tx, twq, ts, tz, out, (int)M, (int)N, (int)K, (int)group, p.splits,
-                         reinterpret_cast<uint8_t*>(workspace));
+                         reinterpret_cast<uint8_t*>(workspace), none);
   if (e != cudaSuccess) return check_cuda(e, "w4a16 tc launch");
   return check_cuda(cudaGetLastError(), "w4a16 tc launch");
+}
+
+// Grouped W4A16 over E experts (the MoE expert GEMMs in one launch): rows of
+// x [rows, K] are grouped by expert, offsets [E + 1] on the device; weights are
+// stacked per expert (qweight [E*K, N/8], scales / zeros [E*K/g, N]).  With
+// glu, N is the hidden width, the second weight set is the up projection and
+// y [rows, N] = SiLU(x.Wg) * (x.Wu); without, y = x.W.
+int w4a16_tc_grouped(const void* x, const int32_t* qw, const void* sc, const void* zr, const int32_t* qw2,
+                     const void* sc2, const void* zr2, const int32_t* offsets, int64_t E, void* y, int64_t rows,
+                     int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream) {
+  using namespace tc;
+  const bool glu = qw2 != nullptr;
+  if (!workspace || workspace_bytes < (size_t)HEADER_BYTES)
+    return fail(B200Q_ERR_WORKSPACE, "w4a16 grouped: workspace of " + std::to_string(HEADER_BYTES) + " bytes required");
+  if (rows == 0) return B200Q_OK;
+  const CUtensorMapDataType h16 = CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const uint32_t wbox = glu ? BN / 16 : BN / 8, cbox = glu ? BN / 2 : BN;
+  const uint32_t srows = glu ? 1 : (group >= BK ? 1 : (uint32_t)(BK / group));
+  const uint64_t krows = (uint64_t)E * K, grows = (uint64_t)E * (K / group);
+  CUtensorMap tx, twq, ts, tz;
+  Grouped g = {};
+  int rc;
+  if ((rc = encode_2d(&tx, h16, x, K, rows, (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  auto enc_w = [&](CUtensorMap* wm, CUtensorMap* sm, CUtensorMap* zm, const int32_t* q, const void* s_,
+                   const void* z_) -> int {
+    int r;
+    if ((r = encode_2d(wm, CU_TENSOR_MAP_DATA_TYPE_INT32, q, N / 8, krows, (uint64_t)N / 2, wbox, BK,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return r;
+    if ((r = encode_2d(sm, h16, s_, N, grows, (uint64_t)N * 2, cbox, srows, CU_TENSOR_MAP_SWIZZLE_NONE))) return r;
+    return encode_2d(zm, h16, z_, N, grows, (uint64_t)N * 2, cbox, srows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  };
+  if ((rc = enc_w(&twq, &ts, &tz, qw, sc, zr))) return rc;
+  if (glu && (rc = enc_w(&g.wq2, &g.s2, &g.z2, qw2, sc2, zr2))) return rc;
+  g.offsets = offsets;
+  g.E = (int)E;
+  const bool bf = dtype == B200Q_DTYPE_BF16;
+  auto kern = glu ? (bf ? w4a16_tc_kernel<true, 1, MODE_GLU> : w4a16_tc_kernel<false, 1, MODE_GLU>)
+                  : (bf ? w4a16_tc_kernel<true, 1, MODE_GROUPED> : w4a16_tc_kernel<false, 1, MODE_GROUPED>);
+  const uint32_t smem = Cfg<1>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 grouped)");
+  // every expert's rows in 128-row tiles: at most rows/128 + E tiles
+  const int tiles_m = (int)((rows + BM - 1) / BM + E);
+  const int tiles_n = (int)((N + (glu ? BN / 2 : BN) - 1) / (glu ? BN / 2 : BN));
+  OutSet out = single_out(y, N);
+  kern<<<dim3(tiles_n, tiles_m, 1), THREADS, smem, stream>>>(tx, twq, ts, tz, out, (int)rows, (int)N, (int)K,
+                                                             (int)group, 1, reinterpret_cast<uint8_t*>(workspace), g);
+  return check_cuda(cudaGetLastError(), "w4a16 grouped launch");
 }
 
 }  // namespace b200q

@@ -50,9 +50,17 @@ class QuantizedMoE(nn.Module):
             up_q, up_s, up_z            (same shapes as gate),
             down_q [E, H, D/8], down_s [E, H/g, D], down_z) -> [T, D]
 
-    Experts run one after another on contiguous row blocks of the routed
-    tokens (the routing kernel groups them); the expert row counts are read on
-    the host once per call to size those launches."""
+    All experts run in two launches over the routed rows (grouped by expert
+    by the routing kernel): the gate and up projections with SiLU * mul fused
+    into the epilogue, then the down projection.  The expert row counts stay
+    on the device, so a call has no host synchronisation and can be captured
+    in a CUDA graph.  ``grouped=False`` runs the experts one at a time with
+    separate gate / up / silu_mul / down launches (row counts read on the
+    host), the unfused form kept for comparison."""
+
+    def __init__(self, grouped: bool = True):
+        super().__init__()
+        self.grouped = grouped
 
     def forward(self, x, router_logits, gate_q, gate_s, gate_z, up_q, up_s, up_z, down_q, down_s, down_z):
         T, D = x.shape
@@ -61,6 +69,10 @@ class QuantizedMoE(nn.Module):
         gd = down_q.shape[1] // down_s.shape[1]
         topi, gates, offsets, slot_token, token_slot = ops.moe_route(router_logits.to(x.dtype))
         xg = ops.moe_gather(x, slot_token)
+        if self.grouped:
+            h = ops.moe_grouped_gemm(xg, offsets, gate_q, gate_s, gate_z, g, up=(up_q, up_s, up_z))
+            ye = ops.moe_grouped_gemm(h, offsets, down_q, down_s, down_z, gd)
+            return ops.moe_combine(ye, token_slot, gates)
         offs = offsets.cpu().tolist()
         ye = torch.empty((2 * T, D), dtype=x.dtype, device=x.device)
         for e in range(E):

@@ -212,6 +212,39 @@ def moe_route(router_logits: torch.Tensor):
     return topi, gates, offsets, slot_token, token_slot
 
 
+def moe_grouped_gemm(x: torch.Tensor, offsets: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                     zeros: torch.Tensor, group: int, up=None) -> torch.Tensor:
+    """One launch over all experts.  x [rows, K] grouped by expert (rows of
+    expert e at [offsets[e], offsets[e+1]), offsets on the device); qweight
+    [E, K, N/8], scales / zeros [E, K/group, N].  Returns y [rows, N] =
+    x . W_e, or with ``up = (qweight_up, scales_up, zeros_up)`` the fused
+    SiLU(x . Wg_e) * (x . Wu_e)."""
+    if not x.is_cuda:
+        raise RuntimeError("b200q moe_grouped_gemm runs on CUDA tensors only")
+    rows, K = x.shape
+    E = qweight.shape[0]
+    if qweight.dim() != 3 or qweight.shape[1] != K or qweight.dtype != torch.int32:
+        raise ValueError("qweight must be int32 [E, K, N/8]")
+    N = qweight.shape[2] * 8
+    if offsets.dtype != torch.int32 or offsets.numel() != E + 1:
+        raise ValueError("offsets must be int32 [E + 1]")
+    dt = _dtype_code(x.dtype)
+    ts = [_aligned(t) for t in (x, qweight, scales.to(x.dtype), zeros.to(x.dtype), offsets)]
+    if up is not None:
+        ts += [_aligned(up[0]), _aligned(up[1].to(x.dtype)), _aligned(up[2].to(x.dtype))]
+        if tuple(ts[5].shape) != tuple(qweight.shape):
+            raise ValueError("up-projection qweight must match the gate's shape")
+    y = torch.empty((rows, N), dtype=x.dtype, device=x.device)
+    if rows == 0:
+        return y
+    ws = workspace(x.device, 256)
+    ptr = lambda i: ts[i].data_ptr() if i < len(ts) else None  # noqa: E731
+    _lib.check(_lib.lib().b200q_moe_grouped_gemm(ptr(0), ptr(1), ptr(2), ptr(3), ptr(5), ptr(6), ptr(7), ptr(4), E,
+                                                 y.data_ptr(), rows, N, K, group, dt, ws.data_ptr(), ws.numel(),
+                                                 _stream_ptr(x.device)))
+    return y
+
+
 def moe_gather(x: torch.Tensor, slot_token: torch.Tensor) -> torch.Tensor:
     x = _aligned(x)
     xg = torch.empty((slot_token.numel(), x.shape[1]), dtype=x.dtype, device=x.device)
