@@ -326,6 +326,35 @@ def run_siblings(device, steps, warmup, sampler):
     return out
 
 
+def run_siblings_multi(world, rank, device, steps, warmup, sampler):
+    """Expert-parallel MoE (Mixtral shape, T=512 tokens split evenly over the
+    ranks, E/P experts per rank): route locally, NCCL all-to-all dispatch,
+    grouped W4A16 experts, all-to-all return, gated combine.  Eager launches
+    (the all-to-all split sizes are read on the host), CUDA events, max over
+    ranks."""
+    from kernelbench_harbor_b200 import parallel
+    T, D, H, E = 512, 4096, 14336, 8
+    tl, epr = T // world, E // world
+    g = torch.Generator(device=device).manual_seed(300)
+    x = torch.randn(T, D, generator=g, device=device).half()
+    logits = (x.float() @ (torch.randn(E, D, generator=g, device=device) * 0.02).t()).half()
+    x, logits = x[rank * tl:(rank + 1) * tl].contiguous(), logits[rank * tl:(rank + 1) * tl].contiguous()
+    ws = []
+    for j, (kk, nn) in enumerate(((D, H), (D, H), (H, D))):
+        q, s_, z = [], [], []
+        for e in range(rank * epr, (rank + 1) * epr):
+            qe, se, ze = make_weights(400 + 10 * e + 3 * j, device, K=kk, N=nn)
+            q.append(qe), s_.append(se), z.append(ze)
+        ws += [torch.stack(q), torch.stack(s_), torch.stack(z)]
+    mod = parallel.ExpertParallelMoE(E)
+    msteps = max(3, min(steps, 20))
+    us = time_calls(lambda i: mod(x, logits, ws), 1, msteps, warmup, world, sampler, False) * 1e3
+    fl = T * 2 * 3 * 2 * D * H
+    return {"moe_ep_top2_t512": {"us_per_call": round(us, 1), "TFLOP_s": round(fl / us / 1e6, 1),
+                                 "experts_per_gpu": epr, "tokens_per_gpu": tl, "steps": msteps,
+                                 "timing": "eager launches, CUDA events, max over ranks"}}
+
+
 # ---------------------------------------------------------------------------- CPU legs
 def cpu_reference_time(M, steps, warmup, budget_s=0.25):
     """Median seconds of one full call of the reference op sequence on the host
@@ -402,6 +431,8 @@ def main():
     siblings = None
     if world == 1 and not args.no_siblings:
         siblings = run_siblings(device, args.steps, args.warmup, ClockSampler(device.index))
+    elif world > 1 and not args.no_siblings:
+        siblings = run_siblings_multi(world, rank, device, args.steps, args.warmup, ClockSampler(device.index))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -21,6 +21,9 @@
 #ifndef B200Q_WAIT_SLEEP_NS
 #define B200Q_WAIT_SLEEP_NS 100000  // suspend-time hint of mbarrier waits in ns (0: plain polling)
 #endif
+#ifndef B200Q_WAIT_BACKOFF_NS
+#define B200Q_WAIT_BACKOFF_NS 0  // sleep between unsuccessful polls in ns (0: none)
+#endif
 #ifndef B200Q_WAIT_NS
 #define B200Q_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait in these kernels
 #endif
@@ -252,6 +255,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 #else
     if (mbar_try_wait(bar, parity)) return true;
 #endif
+#if B200Q_WAIT_BACKOFF_NS > 0
+    __nanosleep(B200Q_WAIT_BACKOFF_NS);
+#endif
     if ((i & 63) == 0) {
       const uint64_t t = globaltimer();
       if (i == 0) {
@@ -276,6 +282,23 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Contiguous global -> shared copy of `bytes` (a multiple of 16, both
+// addresses 16-byte aligned) by the bulk-copy engine, completion counted on
+// `bar`.  No multicast.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy view of global memory (data
+// another CTA published) before its later async-proxy (bulk copy) reads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // Same with an L2 eviction-priority hint (createpolicy result).
@@ -472,6 +495,17 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
                "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
+}
+// 32 lanes x 32 consecutive columns
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 }  // namespace b200q

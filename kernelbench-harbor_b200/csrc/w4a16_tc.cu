@@ -29,137 +29,10 @@
 // which yields columns (0,4), (1,5), (2,6), (3,7) of a word; the B operand is
 // stored in that column order and the epilogue undoes the permutation in
 // registers.
-#include "common.cuh"
+#include "w4a16_dq.cuh"
 
 namespace b200q {
 namespace tc {
-
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int NDQ = 16;         // dequantising (and epilogue) warps
-constexpr int WPR = NDQ / 8;    // warps per row-in-group position
-constexpr int WORDS = 8 / WPR;  // packed words per thread per stage
-constexpr int W_PROD = 0, W_MMA = 1, W_XPROD = 2, W_DQ0 = 3;  // warp roles
-constexpr int THREADS = (W_DQ0 + NDQ) * 32;
-constexpr uint32_t XB_BYTES = BM * BK * 2;         // one 128-row x box: 16 KB
-constexpr uint32_t WQ_BYTES = BK * (BN / 8) * 4;   // 8 KB
-constexpr uint32_t SZ_BYTES = 2 * BN * 2;          // up to 2 scale rows per stage (group 32)
-constexpr uint32_t B_BYTES = BK * BN * 2;          // 32 KB
-constexpr int HEADER_BYTES = 256;
-constexpr int MAX_SPLITS = 8;  // portable cluster size
-
-#ifndef B200Q_TC1_SX
-#define B200Q_TC1_SX 4
-#endif
-#ifndef B200Q_TC1_SW
-#define B200Q_TC1_SW 6
-#endif
-#ifndef B200Q_TC1_S2
-#define B200Q_TC1_S2 3
-#endif
-
-// MB = number of 128-row blocks of x per CTA sharing each dequantised B tile
-// (1: 128 x 256 tile, 256 TMEM columns; 2: 256 x 256 tile, all 512 columns).
-template <int MB>
-struct Cfg {
-  static constexpr int SX = MB == 1 ? B200Q_TC1_SX : 3;  // x ring (held until the MMAs of the stage complete)
-  static constexpr int SW = MB == 1 ? B200Q_TC1_SW : 4;  // packed-weight + scale/zero ring (held until dequantised)
-  static constexpr int S2 = MB == 1 ? B200Q_TC1_S2 : 2;  // dequantised-B ring
-  static constexpr uint32_t X_BYTES = MB * XB_BYTES;
-  static constexpr uint32_t OFF_X = 0;
-  static constexpr uint32_t OFF_B = OFF_X + SX * X_BYTES;
-  static constexpr uint32_t OFF_WQ = OFF_B + S2 * B_BYTES;
-  static constexpr uint32_t OFF_S = OFF_WQ + SW * WQ_BYTES;
-  static constexpr uint32_t OFF_Z = OFF_S + SW * SZ_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_Z + SW * SZ_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t TMEM_COLS = MB * BN;
-  static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert((2 * SX + 2 * SW + 2 * S2 + 1) * 8 + 4 <= 256, "barrier area");
-};
-
-template <bool BF16>
-struct DT;
-template <>
-struct DT<false> {
-  using T = __half;
-};
-template <>
-struct DT<true> {
-  using T = __nv_bfloat16;
-};
-
-__device__ __forceinline__ uint32_t as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ __half2 as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
-__device__ __forceinline__ __nv_bfloat162 as_b2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
-
-// Per-thread constants for the 8 columns of one packed word in one group:
-// scale pairs and zero-point terms in the (0,4)(1,5)(2,6)(3,7) pair order.
-struct ColQ {
-  uint32_t s[4], z[4];
-};
-
-template <bool BF16>
-__device__ __forceinline__ ColQ load_colq(const uint8_t* s_row, const uint8_t* z_row, int lane) {
-  const uint4 sv = *reinterpret_cast<const uint4*>(s_row + lane * 16);
-  const uint4 zv = *reinterpret_cast<const uint4*>(z_row + lane * 16);
-  ColQ q;
-  q.s[0] = prmt(sv.x, sv.z, 0x5410);
-  q.s[1] = prmt(sv.x, sv.z, 0x7632);
-  q.s[2] = prmt(sv.y, sv.w, 0x5410);
-  q.s[3] = prmt(sv.y, sv.w, 0x7632);
-  const uint32_t z04 = prmt(zv.x, zv.z, 0x5410), z15 = prmt(zv.x, zv.z, 0x7632);
-  const uint32_t z26 = prmt(zv.y, zv.w, 0x5410), z37 = prmt(zv.y, zv.w, 0x7632);
-  if (!BF16) {
-    const __half2 k1024 = __float2half2_rn(1024.f);
-    const __half2 m1 = __float2half2_rn(-1.f), m64 = __float2half2_rn(-64.f);
-    q.z[0] = as_u32(__hadd2(as_h2(z04), k1024));   // 1024 + z
-    q.z[1] = as_u32(__hfma2(as_h2(z15), m1, m64));  // -(64 + z)
-    q.z[2] = as_u32(__hadd2(as_h2(z26), k1024));
-    q.z[3] = as_u32(__hfma2(as_h2(z37), m1, m64));
-  } else {
-    const __nv_bfloat162 k128 = __float2bfloat162_rn(128.f);
-    q.z[0] = as_u32(__hadd2(as_b2(z04), k128));
-    q.z[1] = as_u32(__hadd2(as_b2(z15), k128));
-    q.z[2] = as_u32(__hadd2(as_b2(z26), k128));
-    q.z[3] = as_u32(__hadd2(as_b2(z37), k128));
-  }
-  return q;
-}
-
-// One packed word -> 8 dequantised values in pair order (n0,n4)(n1,n5)(n2,n6)(n3,n7).
-// fp16: 0x6400|n is 1024+n and 0x6400|(n<<4) is 1024+16n, so the odd positions
-// use an exact fma by 1/16; (n - z) is exact and the multiply by s is the one
-// rounding, as in the reference.  bf16: 0x4300|n is 128+n.
-template <bool BF16>
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, const ColQ& q) {
-  uint4 o;
-  if (!BF16) {
-    const __half2 r16 = __float2half2_rn(0.0625f);
-    const uint32_t w8 = w >> 8;
-    const __half2 h0 = __hsub2(as_h2(and_or(w, 0x000F000Fu, 0x64006400u)), as_h2(q.z[0]));
-    const __half2 h1 = __hfma2(as_h2(and_or(w, 0x00F000F0u, 0x64006400u)), r16, as_h2(q.z[1]));
-    const __half2 h2 = __hsub2(as_h2(and_or(w8, 0x000F000Fu, 0x64006400u)), as_h2(q.z[2]));
-    const __half2 h3 = __hfma2(as_h2(and_or(w8, 0x00F000F0u, 0x64006400u)), r16, as_h2(q.z[3]));
-    o.x = as_u32(__hmul2_rn(h0, as_h2(q.s[0])));
-    o.y = as_u32(__hmul2_rn(h1, as_h2(q.s[1])));
-    o.z = as_u32(__hmul2_rn(h2, as_h2(q.s[2])));
-    o.w = as_u32(__hmul2_rn(h3, as_h2(q.s[3])));
-  } else {
-    const __nv_bfloat162 h0 = __hsub2(as_b2(and_or(w, 0x000F000Fu, 0x43004300u)), as_b2(q.z[0]));
-    const __nv_bfloat162 h1 = __hsub2(as_b2(and_or(w >> 4, 0x000F000Fu, 0x43004300u)), as_b2(q.z[1]));
-    const __nv_bfloat162 h2 = __hsub2(as_b2(and_or(w >> 8, 0x000F000Fu, 0x43004300u)), as_b2(q.z[2]));
-    const __nv_bfloat162 h3 = __hsub2(as_b2(and_or(w >> 12, 0x000F000Fu, 0x43004300u)), as_b2(q.z[3]));
-    o.x = as_u32(__hmul2_rn(h0, as_b2(q.s[0])));
-    o.y = as_u32(__hmul2_rn(h1, as_b2(q.s[1])));
-    o.z = as_u32(__hmul2_rn(h2, as_b2(q.s[2])));
-    o.w = as_u32(__hmul2_rn(h3, as_b2(q.s[3])));
-  }
-  return o;
-}
-
-// B-operand slot -> actual column within each group of 8
-__device__ __forceinline__ int slot_col(int p) { return ((p & 1) << 2) | (p >> 1); }
 
 // Grouped (per-expert) operation: blockIdx.y enumerates the 128-row tiles of
 // every expert's contiguous row block [offsets[e], offsets[e+1]) of x (the
@@ -341,41 +214,56 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int dw = warp - W_DQ0;
     const int nb = lane >> 3, ch = lane & 7;
     const int rr = dw & 7;  // row within each 8-row group
+    static_assert(WPR == 2, "a thread's words i < WORDS/2 lie in K rows 0..31 of the stage, the rest in 32..63");
+    // loop-invariant parts of every address; ring slots and phases advance
+    // incrementally (no divisions in the loop)
+    const uint32_t* wq_t = reinterpret_cast<const uint32_t*>(smem + OFF_WQ) +
+                           (GLU ? (lane >> 4) * (BK * 16) + (rr + 8 * (dw >> 3)) * 16 + (lane & 15)
+                                : (rr + 8 * (dw >> 3)) * 32 + lane);
+    constexpr int WQ_ROW_STEP = GLU ? 8 * WPR * 16 : 8 * WPR * 32;  // words between a thread's words i, i+1
+    uint8_t* b_t = smem + OFF_B + ((dw >> 3) * 4 + nb) * 1024 + rr * 128 + ((ch ^ rr) << 4);
+    int s = 0, j = 0;
+    uint32_t ph_w = 0, ph_b = 1;
     for (int it = 0; it < nk; ++it) {
-      const int s = it % SW, j = it % S2;
-      if (!mbar_wait(&w_full[s], (it / SW) & 1, status)) {
+      if (!mbar_wait(&w_full[s], ph_w, status)) {
         s_err = 1;
         break;
       }
-      if (it >= S2 && !mbar_wait(&b_empty[j], ((it / S2) - 1) & 1, status)) {
+      if (it >= S2 && !mbar_wait(&b_empty[j], ph_b, status)) {
         s_err = 1;
         break;
       }
-      const uint32_t* wq = reinterpret_cast<const uint32_t*>(smem + OFF_WQ + s * WQ_BYTES);
       const uint8_t* srow0 = smem + OFF_S + s * SZ_BYTES;
       const uint8_t* zrow0 = smem + OFF_Z + s * SZ_BYTES;
-      uint8_t* bslot = smem + OFF_B + j * B_BYTES;
       // packed words and scale/zero constants go to registers first, so the
-      // weight slot is released before the dequantised stores start
+      // weight slot is released before the dequantised stores start; with
+      // group 32 the stage's second scale row serves K rows 32..63 (words
+      // i >= WORDS/2), otherwise q1 is q0
       const ColQ q0 = load_colq<BF16>(srow0, zrow0, lane);
       const ColQ q1 = srows > 1 ? load_colq<BF16>(srow0 + BN * 2, zrow0 + BN * 2, lane) : q0;
+      const uint32_t* wq = wq_t + s * (WQ_BYTES / 4);
       uint32_t wv[WORDS];
 #pragma unroll
-      for (int i = 0; i < WORDS; ++i) {
-        const int row = rr + 8 * (WPR * i + (dw >> 3));
-        wv[i] = GLU ? wq[(lane >> 4) * (BK * 16) + row * 16 + (lane & 15)] : wq[row * 32 + lane];
-      }
+      for (int i = 0; i < WORDS; ++i) wv[i] = wq[i * WQ_ROW_STEP];
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[s]);
+      uint8_t* bt = b_t + j * B_BYTES;
 #pragma unroll
       for (int i = 0; i < WORDS; ++i) {
-        const int kg = WPR * i + (dw >> 3);  // 8-row group 0..7; group 32 switches scale row at kg 4
-        const uint4 v = dequant_word<BF16>(wv[i], (srows > 1 && kg >= 4) ? q1 : q0);
-        *reinterpret_cast<uint4*>(bslot + (kg * 4 + nb) * 1024 + rr * 128 + ((ch ^ rr) << 4)) = v;
+        const uint4 v = dequant_word<BF16>(wv[i], i >= WORDS / 2 ? q1 : q0);
+        *reinterpret_cast<uint4*>(bt + i * (WPR * 4 * 1024)) = v;
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&b_full[j]);
+      if (++s == SW) {
+        s = 0;
+        ph_w ^= 1;
+      }
+      if (++j == S2) {
+        j = 0;
+        ph_b ^= 1;
+      }
     }
 
     // ---------------------------------------------------------------- epilogue: TMEM -> y
@@ -565,6 +453,18 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
 }
 
 }  // namespace tc
+
+// The per-tile schedule is poor when it must use 128-row tiles (two 256-row
+// tiles would not fill the SMs in fewer waves) and cannot split K (the
+// 128-row tiles already fill one wave): the SMs then each run one whole
+// 128-row tile at twice the dequantisation per FLOP.  The persistent
+// stream-K kernel (w4a16_sk.cu) runs such shapes with 256-row tiles spread
+// evenly over all SMs (measured on B200, N = 4096, K = 14336: M = 1024 in
+// 117 us instead of 149 us; every other M tried is as fast or faster here).
+bool w4a16_prefer_stream_k(int64_t M, int64_t N, int64_t K, int device) {
+  const tc::Plan p = tc::plan(M, N, K, num_sms(device));
+  return M > 2 * tc::BM && p.mb == 1 && p.splits == 1;
+}
 
 size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
   return tc::plan(M, N, K, num_sms(device)).ws_bytes;

@@ -158,6 +158,25 @@ class PeerGatherW4A16(nn.Module):
         return y
 
 
+def _grouped_local_experts(rows: torch.Tensor, eid: torch.Tensor, n_local: int, w) -> torch.Tensor:
+    """This rank's experts on the rows it received: stable regroup by local
+    expert, fused gate/up/SiLU grouped GEMM, down grouped GEMM, un-permute."""
+    from . import ops
+    gq, gs, gz, uq, us, uz, dq, ds, dz = w
+    order = torch.argsort(eid, stable=True)
+    xs = rows[order].contiguous()
+    counts = torch.bincount(eid, minlength=n_local)
+    offsets = torch.zeros(n_local + 1, dtype=torch.int32, device=rows.device)
+    offsets[1:] = torch.cumsum(counts, 0)
+    g = gq.shape[1] // gs.shape[1]
+    gd = dq.shape[1] // ds.shape[1]
+    h = ops.moe_grouped_gemm(xs, offsets, gq, gs, gz, g, up=(uq, us, uz))
+    ye = ops.moe_grouped_gemm(h, offsets, dq, ds, dz, gd)
+    out = torch.empty_like(ye)
+    out[order] = ye
+    return out
+
+
 class ExpertParallelMoE(nn.Module):
     """Expert-parallel quantised top-2 MoE: rank r of P holds experts
     [r*E/P, (r+1)*E/P) and its own T/P tokens (data parallel).  Per call:
@@ -171,7 +190,11 @@ class ExpertParallelMoE(nn.Module):
     is the benchmark's expert-parallel configuration (one expert per GPU at 8).
 
     ``route``, ``expert`` and ``combine`` are injectable so the exchange logic
-    runs on CPU ranks in tests; by default they are the library's CUDA ops."""
+    runs on CPU ranks in tests; by default they are the library's CUDA ops,
+    and the local experts run as the grouped W4A16 GEMMs (gate/up with the
+    fused SiLU * mul, then down) over the received rows regrouped by expert,
+    with ``local_weights`` = (gate_q, gate_s, gate_z, up_q, up_s, up_z,
+    down_q, down_s, down_z) stacked over this rank's experts."""
 
     def __init__(self, n_experts: int, process_group: Optional[dist.ProcessGroup] = None,
                  route: Optional[Callable] = None, expert: Optional[Callable] = None,
@@ -213,10 +236,14 @@ class ExpertParallelMoE(nn.Module):
         dist.all_to_all_single(recv_eid, send_eid, rc, sc, group=self.pg)
         # local experts on their rows
         out = torch.empty_like(recv_rows)
-        for el in range(epr):
-            sel = torch.nonzero(recv_eid == r * epr + el).flatten()
-            if sel.numel():
-                out[sel] = self.expert(el, recv_rows[sel].contiguous(), local_weights)
+        if self.expert is None:
+            if recv_rows.shape[0]:
+                out = _grouped_local_experts(recv_rows, (recv_eid - r * epr).long(), epr, local_weights)
+        else:
+            for el in range(epr):
+                sel = torch.nonzero(recv_eid == r * epr + el).flatten()
+                if sel.numel():
+                    out[sel] = self.expert(el, recv_rows[sel].contiguous(), local_weights)
         # return trip, then undo the sort: row j of `back` is pair order[j]
         back = x.new_empty((sum(sc), D))
         dist.all_to_all_single(back, out, sc, rc, group=self.pg)

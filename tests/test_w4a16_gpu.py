@@ -121,6 +121,24 @@ def test_tensor_core_path(ops, M, K, N, group, dtype):
     check_w4a16(y, x, q, s, z, group)
 
 
+@pytest.mark.parametrize("M,K,N,group,dtype", [
+    (768, 2048, 4096, 128, "fp16"),    # 96 128-row tiles: one partial wave, no split-K -> stream-K
+    (1000, 4096, 4096, 64, "bf16"),    # ragged 256-row tiles
+    (1024, 1024, 4096, 32, "fp16"),    # short K: ranges of a few stages, many split tiles
+])
+def test_stream_k_path(ops, M, K, N, group, dtype):
+    """Shapes the persistent stream-K kernel runs (256-row tiles, K stages
+    spread evenly over the SMs, split tiles reduced by their owner)."""
+    x, q, s, z = w4a16_inputs(M, K, N, group, dtype, seed=M + N, device="cuda")
+    y = _run(ops, x, q, s, z, group)
+    check_w4a16(y, x, q, s, z, group)
+    y2 = _run(ops, x, q, s, z, group)
+    assert torch.equal(y, y2)  # deterministic reduction order
+    ws = ops.workspace(torch.device("cuda", torch.cuda.current_device()), 0)
+    torch.cuda.synchronize()
+    assert int(ws.count_nonzero()) == 0, "stream-K left the workspace dirty"
+
+
 def test_tensor_core_full_config(ops):
     """BASELINE config 1 at M=4096 against the fp32 torch reference."""
     x, q, s, z = w4a16_inputs(4096, 14336, 4096, 128, "fp16", seed=4096, device="cuda")
