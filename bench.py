@@ -323,6 +323,50 @@ def run_siblings(device, steps, warmup, sampler):
                             "weight_GB_s": round(wb / us / 1e3, 1), "steps": msteps,
                             "timing": "CUDA graph: route, gather, fused gate/up/SiLU grouped GEMM, "
                                       "down grouped GEMM, combine (no host synchronisation)"}
+    del ws
+    torch.cuda.empty_cache()
+    out.update(run_next_rows(device, steps, warmup, sampler))
+    return out
+
+
+def run_next_rows(device, steps, warmup, sampler):
+    """The reference modules next to the W4A16 path, at one of their own
+    configurations each (generate_tasks.py:351-355, 381-385, 427-431):
+    FUSED_QMOE (mixtral, T=256, int8 weights packed on the GPU every call),
+    FUSED_SILU fp8 (mixtral H=14336, T=512) and multi-LoRA (llama3-8B r16, T=64)."""
+    from kernelbench_harbor_b200.modules import FusedQMoE, FusedSiluFp8, MultiLoRAW4
+    out = {}
+    g = torch.Generator(device=device).manual_seed(500)
+    n = max(3, min(steps, 20))
+    T, D, E, N = 256, 4096, 8, 14336
+    x = torch.randn(T, D, generator=g, device=device).half()
+    qw = torch.randint(-8, 8, (E, D, N), generator=g, device=device, dtype=torch.int8)
+    sc = (torch.randn(E, D // 128, N, generator=g, device=device) * 0.01).half()
+    lg = torch.randn(T, E, generator=g, device=device).half()
+    mod = FusedQMoE()
+    us = time_calls(lambda i: mod(x, qw, sc, lg), 1, n, warmup, 1, sampler, True) * 1e3
+    wb = E * D * N + E * (D // 128) * N * 2
+    out["fused_qmoe_mixtral_t256"] = {"us_per_call": round(us, 1), "weight_GB_s": round(wb / us / 1e3, 1),
+                                      "note": "int8 weights read and packed on the GPU inside every call"}
+    del qw
+    T, H = 512, 14336
+    y = torch.randn(T, 2 * H, generator=g, device=device).half()
+    fs = FusedSiluFp8()
+    us = time_calls(lambda i: fs(y), 1, n, warmup, 1, sampler, True) * 1e3
+    b = T * 2 * H * 2 + T * H * 4
+    out["silu_fp8_mixtral_t512"] = {"us_per_call": round(us, 2), "GB_s": round(b / us / 1e3, 1),
+                                    "hbm_frac": round(b / us / 1e3 / load_peaks()["hbm_gbs"], 3)}
+    T, D, N, r, L = 64, 4096, 4096, 16, 8
+    x = torch.randn(T, D, generator=g, device=device).half()
+    qw = torch.randint(-8, 8, (D, N), generator=g, device=device, dtype=torch.int8)
+    sc = (torch.randn(D // 128, N, generator=g, device=device) * 0.01).half()
+    A = (torch.randn(L, D, r, generator=g, device=device) * 0.02).half()
+    B = (torch.randn(L, r, N, generator=g, device=device) * 0.02).half()
+    ids = torch.randint(0, L, (T,), generator=g, device=device)
+    lm = MultiLoRAW4()
+    us = time_calls(lambda i: lm(x, qw, sc, A, B, ids), 1, n, warmup, 1, sampler, True) * 1e3
+    out["multi_lora_llama3_8b_r16_t64"] = {"us_per_call": round(us, 1),
+                                           "note": "int8 base weight packed on the GPU inside every call"}
     return out
 
 

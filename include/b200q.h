@@ -129,6 +129,42 @@ int b200q_mxfp8_gemm(const void* a, const void* scales_a, const void* b, const v
 int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                              void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* stream);
 
+/* GPU weight packer: 4-bit codes [K, N] (int8, one code per byte, row-major)
+ * -> qweight [K, N/8] int32 packed along N, nibble i of word j = column 8j+i:
+ * the packing loop of QUANT_REF.get_inputs (generate_tasks.py:65-69).
+ * offset 0: codes are unsigned nibbles in [0, 15] (the reference format);
+ * offset 8: codes are signed symmetric int4 in [-8, 7] (FUSED_QMOE_REF and
+ * LORA_REF weights, generate_tasks.py:385, 414), stored as q + 8 so that the
+ * W4A16 kernels with zero point 8 reproduce q * s exactly.  N % 8 == 0,
+ * codes 8-byte aligned.  A code out of range sets B200Q_DEV_ERR_BOUNDS in the
+ * workspace status word (when workspace is non-NULL) and is masked to 4 bits. */
+int b200q_pack_int4(const void* codes, int64_t K, int64_t N, int offset, int32_t* qweight, void* workspace,
+                    void* stream);
+
+/* Fused SiLU * mul + per-group dynamic fp8 quantisation (FUSED_SILU_REF,
+ * generate_tasks.py:321-348).  y [T, 2H] = concat(gate, up) in fp16/bf16
+ * (dtype 0/1), H % 128 == 0.  For each row and group of 128 columns:
+ * act = SiLU(gate) * up in fp32, scale = max(amax|act| / 448, 1e-12),
+ * q = e4m3(clamp(act / scale, +-448)) (round to nearest even).  Outputs, any
+ * of which may be NULL (not all): out_dequant [T, H] fp32 = q * scale (the
+ * reference module's result), q_out [T, H] e4m3 codes, scales_out
+ * [T, H/128] fp32. */
+int b200q_silu_mul_fp8(const void* y, int64_t T, int64_t H, int dtype, float* out_dequant, uint8_t* q_out,
+                       float* scales_out, void* stream);
+
+/* Multi-LoRA (LORA_REF, generate_tasks.py:397-424), the adapter part of
+ * y[t] = x[t] . dequant(W) + (x[t] . A[id_t]) . B[id_t].
+ * shrink: lo [T, r] = x [T, D] . A[id_t] [D, r] per token (A [L, D, r]),
+ * fp32 accumulation, rounded to the activation type.  expand_add:
+ * y [T, N] = base [T, N] + round(lo . B[id_t]) (B [L, r, N]), rounded once;
+ * y may be base.  lora_ids [T] int64; r <= 64.  An id outside [0, L) sets
+ * B200Q_DEV_ERR_BOUNDS (shrink, when workspace is non-NULL) and contributes
+ * zero. */
+int b200q_lora_shrink(const void* x, const void* A, const int64_t* lora_ids, int64_t T, int64_t D, int64_t r,
+                      int64_t L, int dtype, void* lo, void* workspace, void* stream);
+int b200q_lora_expand_add(const void* base, const void* lo, const void* B, const int64_t* lora_ids, int64_t T,
+                          int64_t r, int64_t N, int64_t L, int dtype, void* y, void* stream);
+
 /* Grouped W4A16 GEMM over the experts of a MoE layer, one launch for all
  * experts.  x [rows, K] holds every expert's rows contiguously, expert e's at
  * [offsets[e], offsets[e+1]) (offsets [E+1] int32 on the device, as written

@@ -52,6 +52,12 @@ SIGNATURES = {
     "b200q_moe_grouped_gemm": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64,
                                               _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_sz,
                                               _c_vp]),
+    "b200q_pack_int4": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_vp, _c_vp]),
+    "b200q_silu_mul_fp8": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "b200q_lora_shrink": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_vp,
+                                         _c_vp, _c_vp]),
+    "b200q_lora_expand_add": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64,
+                                             ctypes.c_int, _c_vp, _c_vp]),
     "b200q_peer_barrier": (ctypes.c_int, [_c_vp, ctypes.c_int, ctypes.c_int, _c_vp, _c_vp]),
 }
 

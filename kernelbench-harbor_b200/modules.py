@@ -87,5 +87,72 @@ class QuantizedMoE(nn.Module):
         return ops.moe_combine(ye, token_slot, gates)
 
 
+def _zero_points(like: torch.Tensor, value: float, cache: dict) -> torch.Tensor:
+    key = (tuple(like.shape), like.dtype, like.device)
+    z = cache.get(key)
+    if z is None:
+        z = torch.full(like.shape, value, dtype=like.dtype, device=like.device)
+        cache[key] = z
+    return z
+
+
+class FusedQMoE(nn.Module):
+    """Drop-in for FUSED_QMOE_REF.Model (generate_tasks.py:368-378):
+    forward(x [T, D], qweight [E, D, N] int8 symmetric int4 in [-8, 7],
+    scales [E, D/128, N], router_logits [T, E]) -> [T, N].
+
+    The int8 weights are packed on the GPU each call (they arrive per call) as
+    q + 8 with zero point 8, which dequantises to exactly q * s as the
+    reference does; then the routing kernel, one grouped W4A16 launch over all
+    experts for the routed rows only (the reference computes every expert for
+    every token) and the gated combine with the reference's rounding."""
+
+    def __init__(self):
+        super().__init__()
+        self._zeros: dict = {}
+
+    def forward(self, x, qweight, scales, router_logits):
+        E, D, N = qweight.shape
+        g = D // scales.shape[1]
+        packed = ops.pack_int4(qweight, offset=8)
+        sc = scales.to(x.dtype)
+        zeros = _zero_points(sc, 8.0, self._zeros)
+        topi, gates, offsets, slot_token, token_slot = ops.moe_route(router_logits.to(x.dtype))
+        xg = ops.moe_gather(x, slot_token)
+        ye = ops.moe_grouped_gemm(xg, offsets, packed, sc, zeros, g)
+        return ops.moe_combine(ye, token_slot, gates)
+
+
+class MultiLoRAW4(nn.Module):
+    """Drop-in for LORA_REF.Model (generate_tasks.py:397-424):
+    forward(x [T, D], qweight [D, N] int8 symmetric int4, scales [D/128, N],
+    A [L, D, r], B [L, r, N], lora_ids [T]) -> [T, N]
+    = x . dequant(W) + (x . A[id]) . B[id] per token.  The base GEMM is the
+    W4A16 kernel (weights packed on the GPU as q + 8, zero point 8), the
+    adapters two small gather kernels (shrink, expand + add)."""
+
+    def __init__(self):
+        super().__init__()
+        self._zeros: dict = {}
+
+    def forward(self, x, qweight, scales, A, B, lora_ids):
+        D, N = qweight.shape
+        g = D // scales.shape[0]
+        packed = ops.pack_int4(qweight, offset=8)
+        sc = scales.to(x.dtype)
+        base = ops.w4a16_gemm(x, packed, sc, _zero_points(sc, 8.0, self._zeros), g)
+        lo = ops.lora_shrink(x, A, lora_ids)
+        return ops.lora_expand_add(base, lo, B, lora_ids, out=base)
+
+
+class FusedSiluFp8(nn.Module):
+    """Drop-in for FUSED_SILU_REF.Model (generate_tasks.py:321-348):
+    forward(y [T, 2H]) -> fp32 [T, H], SiLU(gate) * up quantised per 128
+    columns to e4m3 and dequantised, in one kernel pass."""
+
+    def forward(self, y):
+        return ops.silu_mul_fp8(y)
+
+
 # the reference harness imports the replacement as ``ModelNew``
 ModelNew = W4A16Linear

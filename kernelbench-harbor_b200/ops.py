@@ -245,6 +245,72 @@ def moe_grouped_gemm(x: torch.Tensor, offsets: torch.Tensor, qweight: torch.Tens
     return y
 
 
+def pack_int4(codes: torch.Tensor, offset: int = 0) -> torch.Tensor:
+    """4-bit codes [..., N] (int8 / uint8, one per byte) -> int32 [..., N/8]
+    packed along N (nibble i of word j = column 8j + i).  offset 0: unsigned
+    codes in [0, 15]; offset 8: signed int4 in [-8, 7] stored as q + 8 (use
+    zero point 8).  Codes out of range set the device status bit."""
+    if not codes.is_cuda:
+        raise RuntimeError("b200q pack_int4 runs on CUDA tensors only")
+    if codes.dtype not in (torch.int8, torch.uint8):
+        raise TypeError("codes must be int8 or uint8")
+    N = codes.shape[-1]
+    c = _aligned(codes).reshape(-1, N)
+    out = torch.empty(codes.shape[:-1] + (N // 8,), dtype=torch.int32, device=codes.device)
+    ws = workspace(codes.device, 256)
+    _lib.check(_lib.lib().b200q_pack_int4(c.data_ptr(), c.shape[0], N, offset, out.data_ptr(), ws.data_ptr(),
+                                          _stream_ptr(codes.device)))
+    return out
+
+
+def silu_mul_fp8(y: torch.Tensor, codes: bool = False):
+    """FUSED_SILU_REF: y [T, 2H] -> SiLU(gate) * up quantised per 128 columns
+    to e4m3 and dequantised, fp32 [T, H].  With ``codes`` also returns the
+    e4m3 codes (torch.float8_e4m3fn [T, H]) and scales (fp32 [T, H/128])."""
+    if not y.is_cuda:
+        raise RuntimeError("b200q silu_mul_fp8 runs on CUDA tensors only")
+    T, H2 = y.shape
+    H = H2 // 2
+    y = _aligned(y)
+    out = torch.empty((T, H), dtype=torch.float32, device=y.device)
+    q = torch.empty((T, H), dtype=torch.uint8, device=y.device) if codes else None
+    sc = torch.empty((T, H // 128), dtype=torch.float32, device=y.device) if codes else None
+    _lib.check(_lib.lib().b200q_silu_mul_fp8(y.data_ptr(), T, H, _dtype_code(y.dtype), out.data_ptr(),
+                                             q.data_ptr() if codes else None, sc.data_ptr() if codes else None,
+                                             _stream_ptr(y.device)))
+    if codes:
+        return out, q.view(torch.float8_e4m3fn), sc
+    return out
+
+
+def lora_shrink(x: torch.Tensor, A: torch.Tensor, lora_ids: torch.Tensor) -> torch.Tensor:
+    """lo [T, r] = x[t] . A[lora_ids[t]] per token (A [L, D, r]), x's dtype."""
+    T, D = x.shape
+    L, _, r = A.shape
+    ids = lora_ids.to(torch.int64).contiguous()
+    x, A = _aligned(x), _aligned(A.to(x.dtype))
+    lo = torch.empty((T, r), dtype=x.dtype, device=x.device)
+    ws = workspace(x.device, 256)
+    _lib.check(_lib.lib().b200q_lora_shrink(x.data_ptr(), A.data_ptr(), ids.data_ptr(), T, D, r, L,
+                                            _dtype_code(x.dtype), lo.data_ptr(), ws.data_ptr(),
+                                            _stream_ptr(x.device)))
+    return lo
+
+
+def lora_expand_add(base: torch.Tensor, lo: torch.Tensor, B: torch.Tensor, lora_ids: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [T, N] = base + round(lo[t] . B[lora_ids[t]]) (B [L, r, N])."""
+    T, N = base.shape
+    L, r, _ = B.shape
+    ids = lora_ids.to(torch.int64).contiguous()
+    base, lo, B = _aligned(base), _aligned(lo), _aligned(B.to(base.dtype))
+    y = out if out is not None else torch.empty_like(base)
+    _lib.check(_lib.lib().b200q_lora_expand_add(base.data_ptr(), lo.data_ptr(), B.data_ptr(), ids.data_ptr(), T, r,
+                                                N, L, _dtype_code(base.dtype), y.data_ptr(),
+                                                _stream_ptr(base.device)))
+    return y
+
+
 def moe_gather(x: torch.Tensor, slot_token: torch.Tensor) -> torch.Tensor:
     x = _aligned(x)
     xg = torch.empty((slot_token.numel(), x.shape[1]), dtype=x.dtype, device=x.device)

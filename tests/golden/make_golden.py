@@ -204,6 +204,48 @@ def make_fp8(ref_root: str, out: dict):
     out["fp8_block32"] = {"M": M, "K": K, "N": N, "block": B}
 
 
+def make_silu_fp8(ref_root: str, out: dict):
+    """FUSED_SILU_REF (generate_tasks.py:321-348): SiLU * mul + per-128 dynamic
+    e4m3 quantisation, evaluated by the reference module on the CPU."""
+    path = os.path.join(ref_root, "tasks", "fused_silu_fp8", "fused_silu_fp8__deepseek_moe__T256__fp16",
+                        "environment", "reference.py")
+    mod = load_module(path, "ref_silu_fp8")
+    g = torch.Generator().manual_seed(5000)
+    for dtype in ("fp16", "bf16"):
+        T, H = 8, 384
+        y = torch.randn(T, 2 * H, generator=g).to(tdt(dtype))
+        y[0, :H] = 0.0  # an all-zero group: the scale floor
+        y[1, H:H + 128] *= 40.0  # a group whose products are large
+        with torch.no_grad():
+            o = mod.Model()(y)
+        tag = f"silu_fp8_t{T}_h{H}_{dtype}"
+        np.savez_compressed(os.path.join(HERE, tag + ".npz"), y=to_np(y), out=o.numpy())
+        out[tag] = {"T": T, "H": H, "dtype": dtype, "group": mod.GROUP}
+
+
+def make_lora(ref_root: str, out: dict):
+    """LORA_REF (generate_tasks.py:397-424): int4 base + per-token gathered LoRA."""
+    path = os.path.join(ref_root, "tasks", "multi_lora_qgemm", "multi_lora_qgemm__llama3_8b_r16__fp16",
+                        "environment", "reference.py")
+    mod = load_module(path, "ref_lora")
+    g = torch.Generator().manual_seed(6000)
+    T, D, N, r, L = 16, 256, 128, 16, 4
+    x = torch.randn(T, D, generator=g).to(torch.float16)
+    qweight = torch.randint(-8, 8, (D, N), generator=g, dtype=torch.int8)
+    scales = (torch.randn(D // 128, N, generator=g) * 0.01).to(torch.float16)
+    A = (torch.randn(L, D, r, generator=g) * 0.02).to(torch.float16)
+    B = (torch.randn(L, r, N, generator=g) * 0.02).to(torch.float16)
+    ids = torch.randint(0, L, (T,), generator=g)
+    inputs = [x, qweight, scales, A, B, ids]
+    with torch.no_grad():
+        y = mod.Model()(*inputs)
+        y32 = gt_call(mod.Model(), inputs)
+    np.savez_compressed(os.path.join(HERE, "lora_t16_d256_n128_r16.npz"), x=x.numpy(), qweight=qweight.numpy(),
+                        scales=scales.numpy(), A=A.numpy(), B=B.numpy(), lora_ids=ids.numpy(),
+                        y_module=y.numpy(), y_fp32=y32.numpy())
+    out["lora_t16_d256_n128_r16"] = {"T": T, "D": D, "N": N, "r": r, "L": L}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="kernelbench-harbor checkout")
@@ -215,6 +257,8 @@ def main():
     make_w8a8(args.ref, out)
     make_routing(args.ref, out)
     make_fp8(args.ref, out)
+    make_silu_fp8(args.ref, out)
+    make_lora(args.ref, out)
     with open(os.path.join(HERE, "MANIFEST.json"), "w") as f:
         json.dump({"torch": torch.__version__, "cases": out}, f, indent=1, sort_keys=True)
     print(json.dumps(out, indent=1))

@@ -72,6 +72,33 @@ def test_reference_layer_shapes(ops, K, N):
     torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 128), **TOL)
 
 
+# the reference's whole W4A16 task grid (generate_tasks.py:480-489, 534-541):
+# every layer at g64 fp16, g128 fp16 and g128 bf16, decode M=16
+LAYERS = [(4096, 14336), (14336, 4096), (8192, 28672), (28672, 8192), (3584, 18944), (18944, 3584),
+          (8192, 29568), (29568, 8192)]
+
+
+def _gpu_inputs(M, K, N, group, dtype, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    nib = torch.randint(0, 16, (K, N), generator=g, device="cuda", dtype=torch.int32)
+    q = torch.zeros(K, N // 8, dtype=torch.int32, device="cuda")
+    for i in range(8):
+        q |= nib[:, i::8] << (4 * i)
+    dt = torch.float16 if dtype == "fp16" else torch.bfloat16
+    x = torch.randn(M, K, generator=g, device="cuda").to(dt)
+    s = (torch.rand(K // group, N, generator=g, device="cuda") * 0.018 + 0.002).to(dt)
+    z = torch.randint(0, 16, (K // group, N), generator=g, device="cuda").to(dt)
+    return x, q, s, z
+
+
+@pytest.mark.parametrize("K,N", LAYERS)
+@pytest.mark.parametrize("group,dtype", [(64, "fp16"), (128, "fp16"), (128, "bf16")])
+def test_reference_task_grid(ops, K, N, group, dtype):
+    x, q, s, z = _gpu_inputs(16, K, N, group, dtype, seed=K * 7 + N + group)
+    y = _run(ops, x, q, s, z, group)
+    check_w4a16(y, x, q, s, z, group)
+
+
 def test_benchmark_decode_config_vs_oracle(ops):
     """M=16, K=14336, N=4096, g128, against the numpy oracle."""
     x, q, s, z = w4a16_inputs(16, 14336, 4096, 128, "fp16", seed=1016, device="cuda")
