@@ -34,7 +34,7 @@
 namespace b200q {
 namespace tc {
 
-// Grouped (per-expert) operation: blockIdx.y enumerates the 128-row tiles of
+// Grouped (per-expert) operation: blockIdx.y enumerates the 256-row tiles of
 // every expert's contiguous row block [offsets[e], offsets[e+1]) of x (the
 // routing kernel's grouping), expert e's weights are rows [e*K, (e+1)*K) of
 // the stacked qweight (scales / zeros rows [e*K/g, (e+1)*K/g)).  With GLU the
@@ -55,7 +55,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                     const __grid_constant__ OutSet out, int M, int N, int K, int group, int splits, uint8_t* __restrict__ ws,
                     const __grid_constant__ Grouped grp) {
-  static_assert(MODE == MODE_PLAIN || MB == 1, "grouped tiles are 128 rows");
   constexpr bool GLU = MODE == MODE_GLU;
   constexpr int OUTC = GLU ? BN / 2 : BN;  // output columns per tile
   using T = typename DT<BF16>::T;
@@ -80,14 +79,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
   const int n0 = n_tile * OUTC;  // first output (and weight) column of the tile
   int m0 = m_tile * BM * MB, m_end = M, wk0 = 0;
+  int mb_act = MB;  // 128-row blocks of the tile that hold rows (grouped: an expert's last tile may need one)
   if (MODE != MODE_PLAIN) {
     // find this CTA's expert and row tile; CTAs past the last tile exit
     int e = 0, t = m_tile;
     for (; e < grp.E; ++e) {
       const int a = grp.offsets[e], b = grp.offsets[e + 1];
-      const int tiles = (b - a + BM - 1) / BM;
+      const int tiles = (b - a + BM * MB - 1) / (BM * MB);
       if (t < tiles) {
-        m0 = a + t * BM;
+        m0 = a + t * BM * MB;
         m_end = b;
         break;
       }
@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (e == grp.E) return;
     wk0 = e * K;
+    mb_act = min(MB, (m_end - m0 + BM - 1) / BM);
   }
   const int nk_total = (K + BK - 1) / BK;
   const int k_begin = (int)((long long)split * nk_total / splits);
@@ -174,10 +175,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         const int kb = (k_begin + it) * BK;
-        mbar_arrive_expect_tx(&x_full[s], X_BYTES);
+        mbar_arrive_expect_tx(&x_full[s], mb_act * XB_BYTES);
 #pragma unroll
         for (int mb = 0; mb < MB; ++mb)
-          tma_load_2d(smem + OFF_X + s * X_BYTES + mb * XB_BYTES, &tm_x, kb, m0 + mb * BM, &x_full[s]);
+          if (mb < mb_act)
+            tma_load_2d(smem + OFF_X + s * X_BYTES + mb * XB_BYTES, &tm_x, kb, m0 + mb * BM, &x_full[s]);
       }
     }
   } else if (warp == W_MMA) {
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t bd = smem_desc(bb + kk * 8192, 1024, 4096, 2);
 #pragma unroll
           for (int mb = 0; mb < MB; ++mb) {
+            if (mb >= mb_act) break;
             const uint64_t ad = smem_desc(xa + mb * XB_BYTES + kk * 32, 16, 1024, 2);
             tc_mma_f16_ss(tmem + mb * BN, ad, bd, idesc, (it | kk) != 0);
           }
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           // up columns sit 128 TMEM columns to the right; h = SiLU(g) * u with
           // g and u rounded to the activation type first and one rounding of
           // the product, as the unfused gate/up GEMMs + silu_mul compute it
-          tmem_ld32(tl + ocol + BN / 2, r);
+          tmem_ld32(tl + acc * BN + ocol + BN / 2, r);
           tmem_ld_wait();
 #pragma unroll
           for (int p = 0; p < 32; ++p) {
@@ -570,13 +573,16 @@ int w4a16_tc_grouped(const void* x, const int32_t* qw, const void* sc, const voi
   g.offsets = offsets;
   g.E = (int)E;
   const bool bf = dtype == B200Q_DTYPE_BF16;
-  auto kern = glu ? (bf ? w4a16_tc_kernel<true, 1, MODE_GLU> : w4a16_tc_kernel<false, 1, MODE_GLU>)
-                  : (bf ? w4a16_tc_kernel<true, 1, MODE_GROUPED> : w4a16_tc_kernel<false, 1, MODE_GROUPED>);
-  const uint32_t smem = Cfg<1>::SMEM;
+  // 256-row tiles: one dequantised weight tile serves up to 256 of an
+  // expert's rows (the second 128-row block is skipped when the tile has no
+  // more than 128 rows)
+  auto kern = glu ? (bf ? w4a16_tc_kernel<true, 2, MODE_GLU> : w4a16_tc_kernel<false, 2, MODE_GLU>)
+                  : (bf ? w4a16_tc_kernel<true, 2, MODE_GROUPED> : w4a16_tc_kernel<false, 2, MODE_GROUPED>);
+  const uint32_t smem = Cfg<2>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(w4a16 grouped)");
-  // every expert's rows in 128-row tiles: at most rows/128 + E tiles
-  const int tiles_m = (int)((rows + BM - 1) / BM + E);
+  // every expert's rows in 256-row tiles: at most rows/256 + E tiles
+  const int tiles_m = (int)((rows + 2 * BM - 1) / (2 * BM) + E);
   const int tiles_n = (int)((N + (glu ? BN / 2 : BN) - 1) / (glu ? BN / 2 : BN));
   OutSet out = single_out(y, N);
   kern<<<dim3(tiles_n, tiles_m, 1), THREADS, smem, stream>>>(tx, twq, ts, tz, out, (int)rows, (int)N, (int)K,
