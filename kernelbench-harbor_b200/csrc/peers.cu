@@ -113,7 +113,10 @@ int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* sc
   out.ldy = (int)ldy;
   out.col0 = (int)col0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (M >= W4A16_TC_MIN_M && w4a16_prefer_stream_k(M, N, K, -1))
+  // several destinations: the per-tile kernel, whose epilogue stages each tile
+  // and stores whole 512-byte rows (the stream-K kernel stores 64-byte row
+  // pieces, which cross NVLink poorly)
+  if (M >= W4A16_TC_MIN_M && n_peers == 1 && w4a16_prefer_stream_k(M, N, K, -1))
     return w4a16_sk(x, qweight, scales, zeros, out, M, N, K, group, dtype, workspace, workspace_bytes, st);
   if (M >= W4A16_TC_MIN_M)
     return w4a16_tc(x, qweight, scales, zeros, out, M, N, K, group, dtype, workspace, workspace_bytes, st);

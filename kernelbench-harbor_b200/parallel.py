@@ -158,6 +158,18 @@ class PeerGatherW4A16(nn.Module):
         return y
 
 
+def _grouped_experts_at(xs: torch.Tensor, offsets: torch.Tensor, w) -> torch.Tensor:
+    """Grouped gate/up (fused SiLU * mul) and down GEMMs over rows already
+    grouped by local expert (expert e at [offsets[e], offsets[e+1]); rows past
+    offsets[-1] are left untouched in the result)."""
+    from . import ops
+    gq, gs, gz, uq, us, uz, dq, ds, dz = w
+    g = gq.shape[1] // gs.shape[1]
+    gd = dq.shape[1] // ds.shape[1]
+    h = ops.moe_grouped_gemm(xs, offsets, gq, gs, gz, g, up=(uq, us, uz))
+    return ops.moe_grouped_gemm(h, offsets, dq, ds, dz, gd)
+
+
 def _grouped_local_experts(rows: torch.Tensor, eid: torch.Tensor, n_local: int, w) -> torch.Tensor:
     """This rank's experts on the rows it received: stable regroup by local
     expert, fused gate/up/SiLU grouped GEMM, down grouped GEMM, un-permute."""
@@ -198,9 +210,10 @@ class ExpertParallelMoE(nn.Module):
 
     def __init__(self, n_experts: int, process_group: Optional[dist.ProcessGroup] = None,
                  route: Optional[Callable] = None, expert: Optional[Callable] = None,
-                 combine: Optional[Callable] = None):
+                 combine: Optional[Callable] = None, padded: bool = True):
         super().__init__()
         self.E = n_experts
+        self.padded = padded
         self.pg = process_group
         if route is None or combine is None:
             from . import ops
@@ -213,6 +226,66 @@ class ExpertParallelMoE(nn.Module):
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor, local_weights) -> torch.Tensor:
         """x [T_local, D], router_logits [T_local, E]; local_weights is what
         ``expert(e_local, rows, local_weights)`` needs for this rank's experts."""
+        if self.padded:
+            return self._forward_padded(x, router_logits, local_weights)
+        return self._forward_exact_splits(x, router_logits, local_weights)
+
+    def _forward_padded(self, x, router_logits, local_weights):
+        """Exchange with fixed-capacity all-to-alls: every (source, destination)
+        pair gets C = 2 * T_local row slots (the most one rank can send to
+        another), unused slots carry expert id -1.  All counts stay on the
+        device: no host synchronisation, so the whole forward can be captured
+        in a CUDA graph.  Row results equal the exact-split exchange's."""
+        P = dist.get_world_size(self.pg)
+        E, T, D = self.E, x.shape[0], x.shape[1]
+        epr = E // P
+        dev = x.device
+        C = 2 * T
+        topi, gates = self.route(router_logits)
+        pair_e = topi.long().reshape(-1)  # pair j = (token j // 2, choice j % 2)
+        pair_t = torch.arange(2 * T, device=dev) // 2
+        order = torch.argsort(pair_e * (2 * T) + torch.arange(2 * T, device=dev))  # by expert, then pair
+        dest = pair_e[order] // epr
+        # counts by scatter-add (bincount reads its size back to the host)
+        counts = torch.zeros(P, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
+        starts = torch.cumsum(counts, 0) - counts
+        slot = dest * C + torch.arange(2 * T, device=dev) - starts[dest]
+        send = x.new_empty((P * C, D))
+        send[slot] = x[pair_t[order]]
+        send_eid = torch.full((P * C,), -1, dtype=torch.int64, device=dev)
+        send_eid[slot] = pair_e[order] - dest * epr
+        recv = torch.empty_like(send)
+        recv_eid = torch.empty_like(send_eid)
+        dist.all_to_all_single(recv, send, group=self.pg)
+        dist.all_to_all_single(recv_eid, send_eid, group=self.pg)
+        # this rank's experts over the received rows, regrouped by expert (empty slots last)
+        key = torch.where(recv_eid >= 0, recv_eid, torch.full_like(recv_eid, epr))
+        o2 = torch.argsort(key * (P * C) + torch.arange(P * C, device=dev))
+        cnt = torch.zeros(epr + 1, dtype=torch.int64, device=dev).scatter_add_(0, key, torch.ones_like(key))[:epr]
+        offsets = torch.zeros(epr + 1, dtype=torch.int32, device=dev)
+        offsets[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+        rows = recv[o2].contiguous()
+        if self.expert is None:
+            y_sorted = _grouped_experts_at(rows, offsets, local_weights)
+        else:
+            y_sorted = torch.zeros_like(rows)
+            offs = offsets.tolist()
+            for el in range(epr):
+                if offs[el + 1] > offs[el]:
+                    y_sorted[offs[el]:offs[el + 1]] = self.expert(el, rows[offs[el]:offs[el + 1]].contiguous(),
+                                                                  local_weights)
+        y_recv = torch.empty_like(recv)
+        y_recv[o2] = y_sorted
+        back = torch.empty_like(send)
+        dist.all_to_all_single(back, y_recv, group=self.pg)
+        ye = torch.empty((2 * T, D), dtype=x.dtype, device=dev)
+        ye[order] = back[slot]
+        token_slot = torch.arange(2 * T, device=dev, dtype=torch.int32).reshape(T, 2)
+        return self.combine(ye, token_slot, gates)
+
+    def _forward_exact_splits(self, x, router_logits, local_weights):
+        """Exchange with all-to-alls of exactly the routed rows (split sizes
+        read on the host each call)."""
         P = dist.get_world_size(self.pg)
         r = dist.get_rank(self.pg)
         E, T, D = self.E, x.shape[0], x.shape[1]

@@ -32,7 +32,7 @@ def _weights(E, D, H, G, seed):
     return out
 
 
-def _worker(rank, world, port, q_out):
+def _worker(rank, world, port, q_out, padded=True):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -50,7 +50,7 @@ def _worker(rank, world, port, q_out):
         mine = slice(rank * tl, (rank + 1) * tl)
         epr = E // world
         local_w = [t[rank * epr:(rank + 1) * epr].contiguous() for t in w]
-        mod = parallel.ExpertParallelMoE(E)
+        mod = parallel.ExpertParallelMoE(E, padded=padded)
         for _ in range(2):
             y = mod(x[mine].contiguous(), logits[mine].contiguous(), local_w)
         torch.cuda.synchronize()
@@ -64,14 +64,15 @@ def _worker(rank, world, port, q_out):
         dist.destroy_process_group()
 
 
-def test_ep_moe_two_gpus():
+@pytest.mark.parametrize("padded", [True, False])
+def test_ep_moe_two_gpus(padded):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out, padded)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q_out.get(timeout=300) for _ in procs]

@@ -66,7 +66,7 @@ def test_shard_bounds_errors():
     assert parallel.shard_bounds(4096, 8, 7) == (3584, 4096)
 
 
-def _ep_worker(rank, world, port, out):
+def _ep_worker(rank, world, port, out, padded=True):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -91,19 +91,20 @@ def _ep_worker(rank, world, port, out):
 
         epr = E // world
         local_w = mats[rank * epr:(rank + 1) * epr]
-        mod = parallel.ExpertParallelMoE(E, route=route, expert=expert, combine=combine)
+        mod = parallel.ExpertParallelMoE(E, route=route, expert=expert, combine=combine, padded=padded)
         y = mod(xs[rank * T:(rank + 1) * T], logits[rank * T:(rank + 1) * T], local_w)
         out.put((rank, y.numpy()))
     finally:
         dist.destroy_process_group()
 
 
-def test_expert_parallel_matches_dense():
+@pytest.mark.parametrize("padded", [True, False])
+def test_expert_parallel_matches_dense(padded):
     from oracle import moe as om
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q_out, padded)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q_out.get(timeout=120) for _ in range(2))
