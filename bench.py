@@ -104,18 +104,25 @@ class ClockSampler:
             self.nv = None
             self.err = str(e)
 
+    def sample(self):
+        """One sample now (also called right after the timed work is enqueued,
+        while the GPU runs it, so short timed regions get at least one)."""
+        if self.nv is None:
+            return
+        try:
+            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.samples.append(mhz)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
     def _run(self):
         while not self._stop:
             if self.active:
-                try:
-                    mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
-                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                    self.samples.append(mhz)
-                    for bit, name in self.REASONS.items():
-                        if r & bit:
-                            self.reasons.add(name)
-                except Exception:
-                    pass
+                self.sample()
             time.sleep(0.005)
 
     def summary(self):
@@ -176,6 +183,7 @@ def time_calls(fn, n_sets, steps, warmup, world, sampler, use_graph):
         s.record()
         g.replay()
         e.record()
+        sampler.sample()  # the replay is enqueued and running
         torch.cuda.synchronize()
         sampler.active = False
     else:
@@ -185,6 +193,7 @@ def time_calls(fn, n_sets, steps, warmup, world, sampler, use_graph):
         for i in range(steps):
             fn(i % n_sets)
         e.record()
+        sampler.sample()
         torch.cuda.synchronize()
         sampler.active = False
     barrier(world)
