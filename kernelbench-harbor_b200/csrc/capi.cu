@@ -59,6 +59,7 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (rc) return rc;
   if (M == 0) return B200Q_OK;
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16: null pointer argument");
+  if (reinterpret_cast<uintptr_t>(y) & 15) return fail(B200Q_ERR_ALIGN, "w4a16: y must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (M >= W4A16_TC_MIN_M && w4a16_prefer_stream_k(M, N, K, -1))
     return w4a16_sk(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);

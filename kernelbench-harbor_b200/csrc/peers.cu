@@ -98,6 +98,8 @@ int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* sc
   OutSet out = {};
   for (int i = 0; i < n_peers; ++i) {
     if (!y_peers[i]) return fail(B200Q_ERR_SHAPE, "w4a16 peers: null destination");
+    if (reinterpret_cast<uintptr_t>(y_peers[i]) & 15)
+      return fail(B200Q_ERR_ALIGN, "w4a16 peers: destinations must be 16-byte aligned");
     out.y[i] = y_peers[i];
   }
   if (pads) {

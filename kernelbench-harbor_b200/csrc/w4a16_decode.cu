@@ -49,7 +49,8 @@ struct Layout {
   static constexpr int STAGE = QW + X + 2 * SZ;
   static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(STAGE % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
-  static_assert(NCONS * MT * 64 * 32 * 4 <= STAGES * STAGE, "reduction buffer must fit in the ring");
+  static_assert(NCONS * MT * 64 * 32 * 4 + 16 * MT * STRIP_COLS * 2 <= STAGES * STAGE,
+                "reduction buffer and output tile must fit in the ring");
 };
 
 template <bool BF16>
@@ -332,6 +333,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int tile = e >> 2, r = e & 3, om = tile >> 3, t = tile & 7, c = ln & 3;
       return 8 * (nh * 16 + 2 * (2 * c + (r & 1)) + om) + t;
     };
+    // the output block is assembled in shared memory (after the reduction
+    // buffer) and leaves as whole rows of 16-byte chunks: coalesced in HBM and
+    // few, large writes when the destinations are peers over NVLink
+    T* tile = reinterpret_cast<T*>(smem + NCONS * MT * 64 * 32 * 4);
+    auto write_rows = [&]() {
+      for (int e = tid; e < rows_here * (STRIP_COLS / 8); e += THREADS) {
+        const int row = e / (STRIP_COLS / 8), ch = e % (STRIP_COLS / 8);
+        const int gcol = strip * STRIP_COLS + ch * 8;
+        if (gcol >= N) continue;  // N % 32 == 0: a chunk is wholly inside or outside
+        const uint4 v = *reinterpret_cast<const uint4*>(tile + row * STRIP_COLS + ch * 8);
+        for (int o = 0; o < out.n; ++o)
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(out.y[o]) + (size_t)(mchunk * 16 * MT + row) * out.ldy +
+                                    out.col0 + gcol) = v;
+      }
+    };
     if (splits == 1 && out.world > 1) {
       if (tid == 0 && !peer_wait_arrivals(out, status)) s_err = 1;
       __syncthreads();
@@ -344,16 +360,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       float v = 0.f;
 #pragma unroll
       for (int kq = 0; kq < 4; ++kq) v += red[(kq * 2 + nh) * MT * 2048 + rest];
-      if (splits == 1) {
-        const int gcol = strip * STRIP_COLS + col_of(i);
-        if (gcol < N)
-          for (int o = 0; o < out.n; ++o)
-            reinterpret_cast<T*>(out.y[o])[(size_t)(mchunk * 16 * MT + row) * out.ldy + out.col0 + gcol] = (T)v;
-      } else {
+      if (splits == 1)
+        tile[row * STRIP_COLS + col_of(i)] = (T)v;
+      else
         my_slot[i] = v;
-      }
     }
-    if (splits == 1) break;
+    if (splits == 1) {
+      __syncthreads();
+      write_rows();
+      break;
+    }
 
     __threadfence();
     __syncthreads();
@@ -393,15 +409,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           v.z += part[sp].z;
           v.w += part[sp].w;
         }
-      const size_t yoff = (size_t)(mchunk * 16 * MT + row) * out.ldy + out.col0 + strip * STRIP_COLS;
       const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int col = col_of(i + q);
-        if (strip * STRIP_COLS + col < N)
-          for (int o = 0; o < out.n; ++o) reinterpret_cast<T*>(out.y[o])[yoff + col] = (T)vv[q];
-      }
+      for (int q = 0; q < 4; ++q) tile[row * STRIP_COLS + col_of(i + q)] = (T)vv[q];
     }
+    __syncthreads();
+    write_rows();
     if (tid == 0) tickets[strip_id] = 0;  // leave the workspace zeroed for the next call
   } while (0);
   if (out.world > 1) {

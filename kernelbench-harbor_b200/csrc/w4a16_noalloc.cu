@@ -73,6 +73,7 @@ extern "C" int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, c
   if (N <= 0 || K <= 0 || K % group) return fail(B200Q_ERR_SHAPE, "w4a16 noalloc: N, K > 0 and K % group == 0");
   if (N % 32) return fail(B200Q_ERR_ALIGN, "w4a16 noalloc: N must be a multiple of 32");
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16 noalloc: null pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15) return fail(B200Q_ERR_ALIGN, "w4a16 noalloc: y must be 16-byte aligned");
   int device = 0;
   int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice");
   if (rc) return rc;
