@@ -43,7 +43,7 @@ constexpr int MAX_PEERS = 8;
 
 // Rows from which the W4A16 tensor-core (tcgen05) path is used; fewer rows
 // take the mma.sync decode kernel.
-constexpr int64_t W4A16_TC_MIN_M = 33;
+constexpr int64_t W4A16_TC_MIN_M = 17;
 //
 // With world > 1 the kernel also orders itself against the other ranks
 // through their signal pads (64 uint32 words per rank, zero-initialised,

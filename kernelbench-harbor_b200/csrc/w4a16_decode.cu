@@ -7,7 +7,8 @@
 // in the activation dtype exactly as the reference rounds it ((nib - z) exact,
 // one rounding for * s), then multiplied with fp32 accumulation.
 //
-// Design (HBM-bound regime, M <= 32 per launch chunk):
+// Design (HBM-bound regime, M <= 32 per launch chunk; the library routes M >= 17 to the
+// tcgen05 kernels, the allocation-free entry point uses it up to M = 32):
 //  * The N axis is cut into 256-column strips (32 packed words = 128 B per K
 //    row); the K axis of each strip into `splits` contiguous ranges so that
 //    strips x splits ~= one CTA per SM (split-K).

@@ -1,5 +1,5 @@
 // W4A16 group-quantised GEMM on tcgen05 as a persistent kernel with a hybrid
-// data-parallel / stream-K schedule: the compute-bound ("prefill", M >= 33)
+// data-parallel / stream-K schedule: the compute-bound ("prefill", M >= 17)
 // path of the plain GEMM.
 //
 // Same arithmetic, tile and warp roles as the per-tile kernel (w4a16_tc.cu):

@@ -1,5 +1,5 @@
 // W4A16 group-quantised GEMM on the 5th-generation tensor cores (tcgen05):
-// the compute-bound ("prefill", M >= 33) path.
+// the compute-bound ("prefill", M >= 17) path.
 //
 // y[M, N] = x[M, K] . W[K, N],  W[k, n] = (nib(k, n) - z[k/g, n]) * s[k/g, n],
 // reference layout (QUANT_REF, generate_tasks.py:45-61): qweight [K, N/8]
