@@ -354,13 +354,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (splits > 1) {
-    // split-K across the CTAs of this cluster (one per K range): row block
-    // [rank * R, rank * R + R) of the tile is owned by cluster rank `rank`.
-    // Each CTA sends its partial rows to the owners' shared memory (the
-    // pipeline buffers, free once every CTA passed the first cluster barrier),
-    // then every owner sums the S partials in rank order and writes y: the
-    // result does not depend on timing, and no global workspace is used.
-    const uint32_t S = (uint32_t)splits, R = BM / S;
+    // split-K across the CTAs of this cluster (one per K range): rows
+    // [lo(o), lo(o + 1)) of the tile, lo(o) = o * BM / S, are owned by cluster
+    // rank o (S any of 2..8, so the row blocks may differ by one row).  Each
+    // CTA sends its partial rows to the owners' shared memory (the pipeline
+    // buffers, free once every CTA passed the first cluster barrier) at
+    // [sender rank][row - lo(owner)], MAXR rows per sender; then every owner
+    // sums the S partials in rank order and writes y: the result does not
+    // depend on timing, and no global workspace is used.
+    const uint32_t S = (uint32_t)splits, MAXR = (BM + S - 1) / S;
     const uint32_t rank = cluster_ctarank();
     cluster_sync();
     if (warp >= W_DQ0 && !s_err) {
@@ -369,8 +371,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int qd = warp & 3, part = dw >> 2;
       constexpr int COLS = BN / (NDQ / 4);
       const uint32_t trow = qd * 32 + lane;
-      const uint32_t owner = trow / R, lr = trow % R;
-      const uint32_t base = map_shared_rank(smem_u32(smem), owner) + ((rank * R + lr) * BN) * 4;
+      uint32_t owner = trow * S / BM;
+      while ((owner + 1) * BM / S <= trow) ++owner;
+      const uint32_t lr = trow - owner * BM / S;
+      const uint32_t base = map_shared_rank(smem_u32(smem), owner) + ((rank * MAXR + lr) * BN) * 4;
 #pragma unroll 1
       for (int c0 = 0; c0 < COLS; c0 += 32) {
         const int cslot = part * COLS + c0;
@@ -389,17 +393,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     cluster_sync();
     if (!s_err) {
       const float* buf = reinterpret_cast<const float*>(smem);
-      for (int e = threadIdx.x * 4; e < (int)(R * BN); e += THREADS * 4) {
+      const int r0 = (int)(rank * BM / S), nr = (int)((rank + 1) * BM / S) - r0;
+      for (int e = threadIdx.x * 4; e < nr * BN; e += THREADS * 4) {
         const int lr = e / BN, c = e % BN;
         float4 acc4 = reinterpret_cast<const float4*>(buf + lr * BN + c)[0];
         for (uint32_t src = 1; src < S; ++src) {
-          const float4 p4 = reinterpret_cast<const float4*>(buf + (src * R + lr) * BN + c)[0];
+          const float4 p4 = reinterpret_cast<const float4*>(buf + (src * MAXR + lr) * BN + c)[0];
           acc4.x += p4.x;
           acc4.y += p4.y;
           acc4.z += p4.z;
           acc4.w += p4.w;
         }
-        const int row = m0 + (int)(rank * R) + lr, col = n0 + c;
+        const int row = m0 + r0 + lr, col = n0 + c;
         if (row < M && col < N) {
           uint2 packed;
           if (!BF16) {
@@ -443,12 +448,14 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   p.mb = (M > BM && t2 < t1) ? 2 : 1;
   p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
   const int nk = (int)((K + BK - 1) / BK);
-  // split-K: the K ranges of a tile form one thread-block cluster (a power of
-  // two <= 8 so row blocks of 128 / splits split evenly), as many as the SMs
-  // allow, keeping >= 4 stages per range
+  // split-K: the K ranges of a tile form one thread-block cluster (at most 8,
+  // the portable cluster size), as many as the SMs allow, keeping >= 4
+  // stages per range; the launch shrinks it further until every cluster of
+  // the grid is co-resident
   const int fill = sms / (p.tiles_m * p.tiles_n);
-  int sp = 1;
-  while (sp * 2 <= MAX_SPLITS && sp * 2 <= fill && sp * 2 <= nk / 4) sp *= 2;
+  int sp = fill < nk / 4 ? fill : nk / 4;
+  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
+  if (sp < 1) sp = 1;
   if (p.mb == 2) sp = 1;
   p.splits = sp;
   p.ws_bytes = HEADER_BYTES;
@@ -515,7 +522,7 @@ int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const vo
     int active = 0;
     if (cudaOccupancyMaxActiveClusters(&active, kern, &q) == cudaSuccess && active >= p.tiles_m * p.tiles_n) break;
     cudaGetLastError();
-    p.splits /= 2;
+    --p.splits;
   }
   dim3 grid(p.tiles_n, p.tiles_m, p.splits);
   cudaLaunchConfig_t cfg = {};
