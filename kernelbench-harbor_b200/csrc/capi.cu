@@ -6,15 +6,10 @@ size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
 int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);
-size_t w4a16_sk_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
 size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device);
-int w4a16_sk(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
-             int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
-             cudaStream_t stream);
 int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
              int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream);
-bool w4a16_prefer_stream_k(int64_t M, int64_t N, int64_t K, int device);
 
 int w4a16_tc_grouped(const void* x, const int32_t* qw, const void* sc, const void* zr, const int32_t* qw2,
                      const void* sc2, const void* zr2, const int32_t* offsets, int64_t E, void* y, int64_t rows,
@@ -46,8 +41,7 @@ size_t b200q_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t grou
   (void)group;
   if (M <= 0 || N <= 0 || K <= 0) return 256;
   if (M >= b200q::W4A16_TC_MIN_M)
-    return b200q::w4a16_prefer_stream_k(M, N, K, device) ? b200q::w4a16_sk_ws_bytes(M, N, K, device)
-                                                         : b200q::w4a16_tc_ws_bytes(M, N, K, device);
+    return b200q::w4a16_tc_ws_bytes(M, N, K, device);
   return b200q::w4a16_decode_ws_bytes(M, N, K, device);
 }
 
@@ -61,8 +55,6 @@ int b200q_w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, 
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16: null pointer argument");
   if (reinterpret_cast<uintptr_t>(y) & 15) return fail(B200Q_ERR_ALIGN, "w4a16: y must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (M >= W4A16_TC_MIN_M && w4a16_prefer_stream_k(M, N, K, -1))
-    return w4a16_sk(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
   if (M >= W4A16_TC_MIN_M)
     return w4a16_tc(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);
   return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, workspace, workspace_bytes, st);

@@ -21,13 +21,9 @@ namespace b200q {
 int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);
-int w4a16_sk(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
-             int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
-             cudaStream_t stream);
 int w4a16_tc(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
              int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace, size_t workspace_bytes,
              cudaStream_t stream);
-bool w4a16_prefer_stream_k(int64_t M, int64_t N, int64_t K, int device);
 
 namespace {
 
@@ -115,11 +111,6 @@ int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* sc
   out.ldy = (int)ldy;
   out.col0 = (int)col0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // several destinations: the per-tile kernel, whose epilogue stages each tile
-  // and stores whole 512-byte rows (the stream-K kernel stores 64-byte row
-  // pieces, which cross NVLink poorly)
-  if (M >= W4A16_TC_MIN_M && n_peers == 1 && w4a16_prefer_stream_k(M, N, K, -1))
-    return w4a16_sk(x, qweight, scales, zeros, out, M, N, K, group, dtype, workspace, workspace_bytes, st);
   if (M >= W4A16_TC_MIN_M)
     return w4a16_tc(x, qweight, scales, zeros, out, M, N, K, group, dtype, workspace, workspace_bytes, st);
   return w4a16_decode(x, qweight, scales, zeros, out, M, N, K, group, dtype, workspace, workspace_bytes, st);

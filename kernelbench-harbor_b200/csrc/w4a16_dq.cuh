@@ -1,6 +1,5 @@
-// Shared pieces of the tcgen05 W4A16 kernels (the per-launch tile kernel in
-// w4a16_tc.cu and the persistent stream-K kernel in w4a16_sk.cu): tile and
-// ring geometry, the per-column scale / zero constants and the LOP3
+// Shared pieces of the tcgen05 W4A16 kernel (w4a16_tc.cu): tile and ring
+// geometry, the per-column scale / zero constants and the LOP3
 // magic-exponent dequantisation of one packed word.
 #pragma once
 #include "common.cuh"

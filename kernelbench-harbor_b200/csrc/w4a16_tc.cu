@@ -361,10 +361,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     // buffers, free once every CTA passed the first cluster barrier) at
     // [sender rank][row - lo(owner)], MAXR rows per sender; then every owner
     // sums the S partials in rank order and writes y: the result does not
-    // depend on timing, and no global workspace is used.
+    // depend on timing, and no global workspace is used.  A 256-row tile
+    // (MB = 2) is reduced in two passes of one 128-row block each, so the
+    // received partials never exceed S * MAXR rows of fp32.
     const uint32_t S = (uint32_t)splits, MAXR = (BM + S - 1) / S;
     const uint32_t rank = cluster_ctarank();
-    cluster_sync();
+    for (int mb = 0; mb < MB; ++mb) {
+    cluster_sync();  // every CTA is done with its pipeline buffers / the previous pass
     if (warp >= W_DQ0 && !s_err) {
       tc_fence_after();
       const int dw = warp - W_DQ0;
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c0 = 0; c0 < COLS; c0 += 32) {
         const int cslot = part * COLS + c0;
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + cslot, r);
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + mb * BN + cslot, r);
         tmem_ld_wait();
         float v[32];
 #pragma unroll
@@ -389,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           st_cluster_v4(base + (cslot + 4 * p) * 4, v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
       }
     }
-    if (threadIdx.x == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
+    if (mb == 0 && threadIdx.x == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
     cluster_sync();
     if (!s_err) {
       const float* buf = reinterpret_cast<const float*>(smem);
@@ -404,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           acc4.z += p4.z;
           acc4.w += p4.w;
         }
-        const int row = m0 + r0 + lr, col = n0 + c;
+        const int row = m0 + mb * BM + r0 + lr, col = n0 + c;
         if (row < M && col < N) {
           uint2 packed;
           if (!BF16) {
@@ -420,6 +423,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    }  // passes over the 128-row blocks
   }
   if (warp == W_MMA) {
     tc_fence_after();
@@ -439,42 +443,38 @@ struct Plan {
 
 Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   Plan p;
-  // 256-row tiles halve the dequantisation per FLOP but cost ~1.35x a 128-row
-  // tile (measured): pick the tile height with fewer estimated wave-times
   p.tiles_n = (int)((N + BN - 1) / BN);
-  const int64_t tiles1 = ((M + BM - 1) / BM) * p.tiles_n;
-  const int64_t tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * p.tiles_n;
-  const double t1 = (double)((tiles1 + sms - 1) / sms), t2 = 1.35 * (double)((tiles2 + sms - 1) / sms);
-  p.mb = (M > BM && t2 < t1) ? 2 : 1;
-  p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
   const int nk = (int)((K + BK - 1) / BK);
   // split-K: the K ranges of a tile form one thread-block cluster (at most 8,
   // the portable cluster size), as many as the SMs allow, keeping >= 4
   // stages per range; the launch shrinks it further until every cluster of
   // the grid is co-resident
-  const int fill = sms / (p.tiles_m * p.tiles_n);
-  int sp = fill < nk / 4 ? fill : nk / 4;
-  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
-  if (sp < 1) sp = 1;
-  if (p.mb == 2) sp = 1;
-  p.splits = sp;
+  auto split_for = [&](int64_t tiles) {
+    int64_t sp = sms / tiles;
+    if (sp > nk / 4) sp = nk / 4;
+    if (sp > MAX_SPLITS) sp = MAX_SPLITS;
+    return (int)(sp < 1 ? 1 : sp);
+  };
+  // estimated time in 128-row stage-times: waves of tiles x splits CTAs,
+  // each running nk / splits stages; a 256-row tile halves the
+  // dequantisation per FLOP but its stage costs ~1.35x a 128-row one (measured)
+  auto cost = [&](int64_t tiles, int sp, double stage) {
+    const int64_t waves = (tiles * sp + sms - 1) / sms;
+    return stage * (double)waves * (double)((nk + sp - 1) / sp);
+  };
+  const int64_t tiles1 = ((M + BM - 1) / BM) * p.tiles_n;
+  const int64_t tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * p.tiles_n;
+  const int sp1 = split_for(tiles1), sp2 = split_for(tiles2);
+  // (up to M = 256 the 128-row split with one DSMEM pass measured faster
+  // than the 256-row split reduced in two passes: 48.8 vs 51.9 us at M = 256)
+  p.mb = (M > 2 * BM && cost(tiles2, sp2, 1.35) < cost(tiles1, sp1, 1.0)) ? 2 : 1;
+  p.tiles_m = (int)((M + BM * p.mb - 1) / (BM * p.mb));
+  p.splits = p.mb == 2 ? sp2 : sp1;
   p.ws_bytes = HEADER_BYTES;
   return p;
 }
 
 }  // namespace tc
-
-// The per-tile schedule is poor when it must use 128-row tiles (two 256-row
-// tiles would not fill the SMs in fewer waves) and cannot split K (the
-// 128-row tiles already fill one wave): the SMs then each run one whole
-// 128-row tile at twice the dequantisation per FLOP.  The persistent
-// stream-K kernel (w4a16_sk.cu) runs such shapes with 256-row tiles spread
-// evenly over all SMs (measured on B200, N = 4096, K = 14336: M = 1024 in
-// 117 us instead of 149 us; every other M tried is as fast or faster here).
-bool w4a16_prefer_stream_k(int64_t M, int64_t N, int64_t K, int device) {
-  const tc::Plan p = tc::plan(M, N, K, num_sms(device));
-  return M > 2 * tc::BM && p.mb == 1 && p.splits == 1;
-}
 
 size_t w4a16_tc_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
   return tc::plan(M, N, K, num_sms(device)).ws_bytes;

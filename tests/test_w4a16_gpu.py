@@ -149,13 +149,15 @@ def test_tensor_core_path(ops, M, K, N, group, dtype):
 
 
 @pytest.mark.parametrize("M,K,N,group,dtype", [
-    (768, 2048, 4096, 128, "fp16"),    # 96 128-row tiles: one partial wave, no split-K -> stream-K
-    (1000, 4096, 4096, 64, "bf16"),    # ragged 256-row tiles
-    (1024, 1024, 4096, 32, "fp16"),    # short K: ranges of a few stages, many split tiles
+    (768, 2048, 4096, 128, "fp16"),    # 48 256-row tiles x 3-way split
+    (1000, 4096, 4096, 64, "bf16"),    # ragged 256-row tiles, 2-way split
+    (1024, 1024, 4096, 32, "fp16"),    # short K, two scale rows per stage
+    (300, 2048, 768, 128, "fp16"),     # ragged rows and columns, 8-way (or as co-resident) split
 ])
-def test_stream_k_path(ops, M, K, N, group, dtype):
-    """Shapes the persistent stream-K kernel runs (256-row tiles, K stages
-    spread evenly over the SMs, split tiles reduced by their owner)."""
+def test_split_256_row_tiles(ops, M, K, N, group, dtype):
+    """256-row tiles whose K ranges form a cluster: the partial tiles are
+    reduced over DSMEM in two passes of one 128-row block, with uneven row
+    ownership when the cluster size does not divide 128."""
     x, q, s, z = w4a16_inputs(M, K, N, group, dtype, seed=M + N, device="cuda")
     y = _run(ops, x, q, s, z, group)
     check_w4a16(y, x, q, s, z, group)
@@ -163,7 +165,7 @@ def test_stream_k_path(ops, M, K, N, group, dtype):
     assert torch.equal(y, y2)  # deterministic reduction order
     ws = ops.workspace(torch.device("cuda", torch.cuda.current_device()), 0)
     torch.cuda.synchronize()
-    assert int(ws.count_nonzero()) == 0, "stream-K left the workspace dirty"
+    assert int(ws.count_nonzero()) == 0, "the split left the workspace dirty"
 
 
 def test_tensor_core_full_config(ops):
