@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Metric (BASELINE.json): W4A16 g128 GEMM us/call and % of the HBM / tensor
+Metric: W4A16 g128 GEMM us/call and % of the HBM / tensor
 roofline at M = 16 / 128 / 4096, 1-8 GPUs.  The headline workload is the
 benchmark's compute-bound configuration, x fp16 [4096, 14336] . W [14336, 4096]
 (K=14336, N=4096, group 128, asymmetric int4, scales U[0.002, 0.02], zeros
@@ -17,7 +17,7 @@ all ranks' outputs over NVLink (one kernel per rank and call); with
 ``--gather nccl`` the local output is all-gathered over NCCL and permuted.
 
 Timing: W untimed warm-up calls, then exactly K calls captured in a CUDA graph
-(N = 1) or launched eagerly (N > 1), bracketed by barrier + synchronize, timed
+(every N; NCCL collectives are captured too), bracketed by barrier + synchronize, timed
 with CUDA events on the launching stream.  Calls rotate over enough copies of
 the weights (and activations) that the working set exceeds the 126 MB L2, so
 every call streams from HBM.  SM clocks and throttle reasons are sampled with
@@ -215,9 +215,10 @@ def run_ours(args, world, rank, device, peaks):
     if world > 1:
         model = (parallel.PeerGatherW4A16(GROUP) if args.gather == "peer"
                  else parallel.ColumnShardedW4A16(GROUP))
+    parity = {}
     for M in sorted(set(args.sweep) | {args.m}):
         set_bytes = w_bytes + M * K_DIM * 2
-        n_sets = max(2, min(8, -(-2 * L2_BYTES // set_bytes)))  # working set > 2x L2 where 8 sets allow
+        n_sets = max(2, -(-2 * L2_BYTES // set_bytes))  # working set > 2x L2
         sets = []
         for i in range(n_sets):
             q, s_, z = make_weights(1000 + i, device)
@@ -231,6 +232,8 @@ def run_ours(args, world, rank, device, peaks):
             fn = lambda i: ops.w4a16_gemm(*sets[i], GROUP)  # noqa: E731
         ms = time_calls(fn, n_sets, args.steps, args.warmup, world, sampler, use_graph)
         us = ms * 1e3
+        if world > 1:
+            parity[M] = sharded_parity(model, sets[0], world)
         ab = algorithmic_bytes(M, N_DIM, K_DIM, GROUP)
         fl = flops(M, N_DIM, K_DIM)
         t_hbm = ab / (peaks["hbm_gbs"] * 1e9 * world)
@@ -240,6 +243,18 @@ def run_ours(args, world, rank, device, peaks):
                     "TFLOP_s": round(fl / (us * 1e-6) / 1e12, 1), "bound": bound,
                     "roofline_frac": round((t_hbm if bound == "hbm" else t_ten) / (us * 1e-6), 4),
                     "l2": f"{n_sets} rotating input sets of {set_bytes / 2**20:.0f} MiB"}
+        if world == 1 and M <= 16:
+            # the same calls with weight prefetch across the launch boundary
+            # (programmatic dependent launch; weights are never written here)
+            prev = ops.set_weight_prefetch(True)
+            ms_p = time_calls(fn, n_sets, args.steps, args.warmup, world, sampler, use_graph)
+            ops.set_weight_prefetch(prev)
+            us_p = ms_p * 1e3
+            sweep[f"{M}_weight_prefetch"] = {
+                "us_per_call": round(us_p, 3), "GB_s": round(ab / (us_p * 1e-6) / 1e9, 1),
+                "roofline_frac": round(t_hbm / (us_p * 1e-6), 4), "bound": "hbm",
+                "note": "b200q_set_weight_prefetch(1): each call streams its first weight tiles while "
+                        "the previous call finishes", "l2": sweep[M]["l2"]}
         del sets
         torch.cuda.empty_cache()
 
@@ -247,18 +262,27 @@ def run_ours(args, world, rank, device, peaks):
     if not args.no_e2e:
         # the public module with HOST buffers: H2D of every forward input and
         # D2H of y inside the timed region, each step
+        # (N > 1: each rank copies its 1/N of x's rows and its weight shard
+        # from the host, x is all-gathered over NCCL, and each rank reads back
+        # its 1/N of y's rows: the hosts together move x, W and y once)
         M = args.m
         q, s_, z = make_weights(1000, device)
         if world > 1:
             q, s_, z = parallel.shard_weights(q, s_, z, world, rank)
         x = make_x(M, 2000, device)
-        hx, hq, hs, hz = (t.cpu().pin_memory() for t in (x, q, s_, z))
-        hy = torch.empty((M, N_DIM), dtype=torch.float16).pin_memory()
+        rows = slice(rank * M // world, (rank + 1) * M // world)
+        hx = x[rows].contiguous().cpu().pin_memory()
+        hq, hs, hz = (t.cpu().pin_memory() for t in (q, s_, z))
+        hy = torch.empty((rows.stop - rows.start, N_DIM), dtype=torch.float16).pin_memory()
         mod = model if world > 1 else ModelNew()
+        x_full = torch.empty((M, K_DIM), dtype=torch.float16, device=device)
 
         def e2e_step():
             dx, dq, ds, dz = (t.to(device, non_blocking=True) for t in (hx, hq, hs, hz))
-            hy.copy_(mod(dx, dq, ds, dz), non_blocking=True)
+            if world > 1:
+                dist.all_gather_into_tensor(x_full, dx)
+                dx = x_full
+            hy.copy_(mod(dx, dq, ds, dz)[rows], non_blocking=True)
 
         e_steps = max(3, min(args.steps, 20))
         for _ in range(max(args.warmup, 1)):
@@ -274,8 +298,22 @@ def run_ours(args, world, rank, device, peaks):
         e2e = {"value": round(e_ms * 1e3, 3), "unit": "us/call",
                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hx, hq, hs, hz)),
                "d2h_bytes_per_step": hy.numel() * hy.element_size(), "steps": e_steps,
-               "path": "ModelNew.forward" if world == 1 else f"{type(model).__name__}.forward"}
-    return sweep, e2e, sampler.summary()
+               "path": ("ModelNew.forward" if world == 1 else
+                        f"x row shards H2D + NCCL all-gather, {type(model).__name__}.forward")}
+    return sweep, e2e, sampler.summary(), parity
+
+
+def sharded_parity(model, inputs, world) -> bool:
+    """One sharded call against this rank's shard computed by the plain
+    single-GPU entry point (same kernel, same shard shape, hence the same
+    split-K order), all shards gathered over NCCL: bit-identical on every rank."""
+    from kernelbench_harbor_b200 import ops, parallel
+    x, q, s_, z = inputs
+    y = model(x, q, s_, z).clone()
+    ref = parallel.gather_columns(ops.w4a16_gemm(x, q, s_, z, GROUP), world)
+    ok = torch.tensor([1 if torch.equal(y, ref) else 0], device=x.device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return bool(ok.item())
 
 
 def run_siblings(device, steps, warmup, sampler):
@@ -391,6 +429,7 @@ def run_siblings_multi(world, rank, device, steps, warmup, sampler):
     g = torch.Generator(device=device).manual_seed(300)
     x = torch.randn(T, D, generator=g, device=device).half()
     logits = (x.float() @ (torch.randn(E, D, generator=g, device=device) * 0.02).t()).half()
+    x_all, logits_all = x, logits
     x, logits = x[rank * tl:(rank + 1) * tl].contiguous(), logits[rank * tl:(rank + 1) * tl].contiguous()
     ws = []
     for j, (kk, nn) in enumerate(((D, H), (D, H), (H, D))):
@@ -403,7 +442,24 @@ def run_siblings_multi(world, rank, device, steps, warmup, sampler):
     msteps = max(3, min(steps, 20))
     us = time_calls(lambda i: mod(x, logits, ws), 1, msteps, warmup, world, sampler, True) * 1e3
     fl = T * 2 * 3 * 2 * D * H
+    # parity: this rank's tokens against the single-GPU module over all experts
+    from kernelbench_harbor_b200.modules import QuantizedMoE
+    y = mod(x, logits, ws).clone()
+    del ws
+    full = []
+    for j, (kk, nn) in enumerate(((D, H), (D, H), (H, D))):
+        q, s_, z = [], [], []
+        for e in range(E):
+            qe, se, ze = make_weights(400 + 10 * e + 3 * j, device, K=kk, N=nn)
+            q.append(qe), s_.append(se), z.append(ze)
+        full += [torch.stack(q), torch.stack(s_), torch.stack(z)]
+    ref = QuantizedMoE()(x_all, logits_all, *full)[rank * tl:(rank + 1) * tl]
+    ok = torch.tensor([1 if torch.equal(y, ref) else 0], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    del full
+    torch.cuda.empty_cache()
     return {"moe_ep_top2_t512": {"us_per_call": round(us, 1), "TFLOP_s": round(fl / us / 1e6, 1),
+                                 "parity_vs_single_gpu": bool(ok.item()),
                                  "experts_per_gpu": epr, "tokens_per_gpu": tl, "steps": msteps,
                                  "timing": "CUDA graph (fixed-capacity all-to-alls, no host "
                                            "synchronisation), CUDA events, max over ranks"}}
@@ -439,6 +495,55 @@ def cpu_reference_time(M, steps, warmup, budget_s=0.25):
     return per_call, cores, sample
 
 
+def profile_case(args) -> int:
+    """A few untimed calls of one seeded case on one GPU, for ncu:
+
+        ncu --set full --clock-control none -k regex:w4a16 -s 1 -c 1 \\
+            python bench.py --profile w4a16=4096 --calls 2
+    """
+    import kernelbench_harbor_b200 as pkg
+    pkg.build()
+    from kernelbench_harbor_b200 import ops
+    kind, size = args.profile.split("=")
+    size = int(size)
+    device = torch.device("cuda", 0)
+    if kind == "w4a16":
+        q, s_, z = make_weights(1, device)
+        x = make_x(size, 2, device)
+        ops.set_weight_prefetch(args.prefetch)
+        call = lambda: ops.w4a16_gemm(x, q, s_, z, GROUP)  # noqa: E731
+    elif kind == "moe":
+        from kernelbench_harbor_b200.modules import QuantizedMoE
+        T, D, H, E = size, 4096, 14336, 8
+        g = torch.Generator(device=device).manual_seed(3)
+        x = torch.randn(T, D, generator=g, device=device).half()
+        logits = (x.float() @ (torch.randn(E, D, generator=g, device=device) * 0.02).t()).half()
+        ws = []
+        for j, (kk, nn) in enumerate(((D, H), (D, H), (H, D))):
+            parts = [make_weights(10 * e + j, device, K=kk, N=nn) for e in range(E)]
+            ws += [torch.stack([p[i] for p in parts]) for i in range(3)]
+        mod = QuantizedMoE()
+        call = lambda: mod(x, logits, *ws)  # noqa: E731
+    elif kind == "w8a8":
+        from kernelbench_harbor_b200.quant import smoothquant_inputs
+        t = [v.to(device) for v in smoothquant_inputs(size, K_DIM, N_DIM, seed=1)[:4]]
+        call = lambda: ops.w8a8_gemm(*t)  # noqa: E731
+    elif kind == "mxfp8":
+        from kernelbench_harbor_b200.mx import quantize_mxfp8
+        g = torch.Generator().manual_seed(1)
+        a = quantize_mxfp8(torch.randn(size, K_DIM, generator=g).half())
+        b = quantize_mxfp8((torch.randn(N_DIM, K_DIM, generator=g) * 0.02).half())
+        t = [a[0].to(device), a[1].to(device), b[0].to(device), b[1].to(device)]
+        call = lambda: ops.mxfp8_gemm(*t)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown profile kind {kind}")
+    for _ in range(args.calls):
+        call()
+    torch.cuda.synchronize()
+    print("ok")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,8 +556,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-siblings", action="store_true")
+    ap.add_argument("--profile", default=None,
+                    help="KIND=SIZE: run `--calls` untimed calls of one case for a profiler and exit; "
+                         "KIND is w4a16 (SIZE = M), moe (tokens), w8a8 (M), mxfp8 (M)")
+    ap.add_argument("--calls", type=int, default=2)
+    ap.add_argument("--prefetch", action="store_true", help="with --profile: weight prefetch on")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile:
+        return profile_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -481,7 +593,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     device = torch.device("cuda", torch.cuda.current_device())
     peaks = load_peaks()
-    sweep, e2e, clocks = run_ours(args, world, rank, device, peaks)
+    sweep, e2e, clocks, parity = run_ours(args, world, rank, device, peaks)
     siblings = None
     if world == 1 and not args.no_siblings:
         siblings = run_siblings(device, args.steps, args.warmup, ClockSampler(device.index))
@@ -511,8 +623,8 @@ def main():
         roof["peak_source"] = ("measured (MEASURED_PEAKS.json, burst)" if peaks["source"] == "measured"
                                else "fallback") + (f" x {world} GPUs" if world > 1 else "")
         # DRAM bytes (read + write) of one launch of the headline kernel, from
-        # the ncu capture `ncu --set full ... profile_case --m 4096` summarised
-        # in profiles/w4a16_tc_m4096.md; None for workloads not captured
+        # one ncu capture of `bench.py --profile w4a16=4096`; None for
+        # workloads not captured
         roof["traffic"] = NCU_TRAFFIC.get(M)
         line = {"metric": METRIC, "value": us, "unit": "us/call", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
@@ -526,6 +638,9 @@ def main():
                            "l2": head["l2"]},
                 "roofline": roof, "sweep": {str(k): v for k, v in sweep.items()}, "siblings": siblings,
                 "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+                **({"parity": {"w4a16_gather": {str(k): v for k, v in parity.items()},
+                               "ep_moe": (siblings or {}).get("moe_ep_top2_t512", {}).get(
+                                   "parity_vs_single_gpu")}} if world > 1 else {}),
                 # our kernels per step: the GEMM (with the gather fused into it for --gather peer)
                 "gpu_launches": args.steps}
         print(json.dumps(line), flush=True)

@@ -54,6 +54,18 @@ const char* b200q_last_error(void);
  * status if the copy itself fails. */
 int b200q_workspace_status(void* workspace, void* stream);
 
+/* Weight prefetch across kernel boundaries (off by default; process-wide).
+ * When on, the small-M W4A16 kernel (M <= 16, single GPU) is launched with
+ * programmatic dependent launch: it starts while the previous kernel in the
+ * stream is still running and streams its first qweight / scales / zeros
+ * tiles before waiting for that kernel to finish; x is read and y written
+ * only after the wait.  The caller promises that the kernel launched just
+ * before each such call on the same stream does not write that call's
+ * qweight, scales or zeros (true whenever weights are loaded once and reused,
+ * as in inference).  Returns the previous setting.  No counterpart in the
+ * reference, whose operator is a single stand-alone call. */
+int b200q_set_weight_prefetch(int enable);
+
 /* Bytes of zero-initialised workspace b200q_w4a16_gemm needs for this shape on
  * `device` (the split-K decomposition depends on the SM count). */
 size_t b200q_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group, int device);
@@ -128,6 +140,13 @@ int b200q_mxfp8_gemm(const void* a, const void* scales_a, const void* b, const v
  * layouts, requirements and results as b200q_w4a16_gemm. */
 int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                              void* y, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* stream);
+
+/* Device status of the last b200q_w4a16_gemm_noalloc call on the current
+ * device, read from the fixed array's header and cleared, like
+ * b200q_workspace_status (waits for `stream`; 0 = no error, else the device
+ * error bits).  Each noalloc call clears the header first, so read it before
+ * the next call.  No counterpart in the reference. */
+int b200q_w4a16_noalloc_status(void* stream);
 
 /* GPU weight packer: 4-bit codes [K, N] (int8, one code per byte, row-major)
  * -> qweight [K, N/8] int32 packed along N, nibble i of word j = column 8j+i:

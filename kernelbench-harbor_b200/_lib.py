@@ -30,6 +30,7 @@ SIGNATURES = {
     "b200q_version": (ctypes.c_int, []),
     "b200q_last_error": (ctypes.c_char_p, []),
     "b200q_workspace_status": (ctypes.c_int, [_c_vp, _c_vp]),
+    "b200q_set_weight_prefetch": (ctypes.c_int, [ctypes.c_int]),
     "b200q_w4a16_workspace_bytes": (_c_sz, [_c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int]),
     "b200q_w4a16_gemm": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64,
                                         ctypes.c_int, _c_vp, _c_sz, _c_vp]),
@@ -46,6 +47,7 @@ SIGNATURES = {
     "b200q_moe_combine": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp]),
     "b200q_w4a16_gemm_noalloc": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64,
                                                 _c_i64, ctypes.c_int, _c_vp]),
+    "b200q_w4a16_noalloc_status": (ctypes.c_int, [_c_vp]),
     "b200q_w4a16_gemm_peers": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, ctypes.c_int, _c_i64, _c_i64,
                                               _c_vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
                                               _c_vp, _c_sz, _c_vp]),

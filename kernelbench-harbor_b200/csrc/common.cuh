@@ -85,6 +85,9 @@ void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int check_cuda(cudaError_t e, const char* what);
 int num_sms(int device);
+// b200q_set_weight_prefetch: whether small-M kernels may stream their weights
+// before the programmatic-dependent-launch wait
+bool weight_prefetch_enabled();
 int current_device();
 
 // encodes a 2D tiled tensor map; returns 0 or a negative b200q status

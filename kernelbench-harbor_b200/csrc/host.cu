@@ -1,6 +1,7 @@
 // Host-side plumbing shared by every entry point: error strings, device
 // properties, tensor-map encoding through the driver entry point, the device
 // status word.
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -10,6 +11,9 @@
 namespace b200q {
 
 static thread_local std::string g_last_error;
+static std::atomic<int> g_weight_prefetch{0};
+
+bool weight_prefetch_enabled() { return g_weight_prefetch.load(std::memory_order_relaxed) != 0; }
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -100,7 +104,12 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
 
 extern "C" {
 
-int b200q_version(void) { return (0 << 16) | 1; }
+int b200q_version(void) { return (0 << 16) | 2; }
+
+int b200q_set_weight_prefetch(int enable) {
+  const int old = b200q::g_weight_prefetch.exchange(enable ? 1 : 0);
+  return old;
+}
 
 const char* b200q_last_error(void) { return b200q::g_last_error.c_str(); }
 

@@ -21,6 +21,9 @@
 //  * Nothing is allocated or freed: no cudaMalloc/cudaFree and no allocating
 //    library routine.  Each call clears the array's header and split-K tickets
 //    (cudaMemsetAsync on the caller's stream) before the kernel runs.
+//  * A device-side error (a bounded wait that gave up) is recorded in the
+//    array's header word; b200q_w4a16_noalloc_status reads and clears it.  The
+//    next call clears it too, so read it before the next call.
 #include <mutex>
 #include <vector>
 
@@ -72,6 +75,7 @@ extern "C" int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, c
     return fail(B200Q_ERR_UNSUPPORTED, "w4a16 noalloc: group must be 32, 64, 128 or 256");
   if (N <= 0 || K <= 0 || K % group) return fail(B200Q_ERR_SHAPE, "w4a16 noalloc: N, K > 0 and K % group == 0");
   if (N % 32) return fail(B200Q_ERR_ALIGN, "w4a16 noalloc: N must be a multiple of 32");
+  if (N > (1ll << 30) || K > (1ll << 30)) return fail(B200Q_ERR_SHAPE, "w4a16 noalloc: size too large");
   if (!x || !qweight || !scales || !zeros || !y) return fail(B200Q_ERR_SHAPE, "w4a16 noalloc: null pointer");
   if (reinterpret_cast<uintptr_t>(y) & 15) return fail(B200Q_ERR_ALIGN, "w4a16 noalloc: y must be 16-byte aligned");
   int device = 0;
@@ -92,4 +96,14 @@ extern "C" int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, c
   const size_t clear = need < 256 + tickets ? need : 256 + tickets;
   if ((rc = check_cuda(cudaMemsetAsync(scratch, 0, clear, st), "noalloc scratch clear"))) return rc;
   return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, scratch, NOALLOC_SCRATCH_BYTES, st);
+}
+
+extern "C" int b200q_w4a16_noalloc_status(void* stream) {
+  using namespace b200q;
+  int device = 0;
+  int rc = check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+  if (rc) return rc;
+  void* scratch = nullptr;
+  if ((rc = scratch_address(device, &scratch))) return rc;
+  return b200q_workspace_status(scratch, stream);
 }

@@ -337,6 +337,14 @@ def moe_combine(ye: torch.Tensor, token_slot: torch.Tensor, gates: torch.Tensor)
     return y
 
 
+def set_weight_prefetch(enable: bool) -> bool:
+    """Lets small-M W4A16 calls stream their weights while the previous kernel
+    in the stream is still running (programmatic dependent launch).  Only valid
+    when the kernel just before each call does not write that call's weights,
+    scales or zeros.  Process-wide; returns the previous setting."""
+    return bool(_lib.lib().b200q_set_weight_prefetch(1 if enable else 0))
+
+
 def device_status(device: torch.device | None = None) -> int:
     """Reads and clears the device error word of this stream's workspace
     (synchronises the stream).  0 means no kernel reported an error."""

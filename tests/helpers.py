@@ -95,14 +95,16 @@ def torch_ref_module(x, qweight, scales, zeros, group):
 
 
 def check_w4a16(y, x, qweight, scales, zeros, group):
-    """fp16: allclose(1e-2) against the fp32 ground truth.  bf16: the
-    reference module itself rounds the weight to bf16 (8 significant bits), so
-    the output is held to allclose(1e-2) against that module's numerics and,
-    against the fp32 ground truth, to allclose(5e-2) with the absolute part
+    """fp16: allclose(1e-2) against the fp32 ground truth.  bf16 through the
+    decode kernel (M <= 16), which applies the scales in fp32: allclose(1e-2)
+    against the fp32 ground truth as well.  bf16 through the tensor-core kernel,
+    which rounds each weight to bf16 (8 significant bits) exactly as the
+    reference module does: allclose(1e-2) against that module's numerics and,
+    against the fp32 ground truth, allclose(5e-2) with the absolute part
     growing as sqrt(K / 4096) (independent weight roundings add up as a random
     walk over the K products: at K = 29568 the module itself is ~0.09 off)."""
     ref32 = torch_ref_fp32(x, qweight, scales, zeros, group)
-    if x.dtype == torch.float16:
+    if x.dtype == torch.float16 or x.shape[0] < 17:
         torch.testing.assert_close(y.float(), ref32, **TOL)
     else:
         torch.testing.assert_close(y.float(), torch_ref_module(x, qweight, scales, zeros, group), **TOL)
