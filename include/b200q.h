@@ -116,7 +116,8 @@ int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dty
 int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
                       int dtype, void* stream);
 
-/* Bytes of zero-initialised workspace b200q_mxfp8_gemm needs for this shape. */
+/* Bytes of zero-initialised workspace b200q_mxfp8_gemm needs (the status
+ * word: split-K is reduced over DSMEM inside a thread-block cluster). */
 size_t b200q_mxfp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device);
 
 /* MXFP8 block-scaled GEMM: y[M, N] = fp16(A_deq . B_deq^T), A [M, K] and B
@@ -226,6 +227,15 @@ int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* sc
                            int rank, int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Column-sharded MXFP8 GEMM with the all-gather fused into its epilogue: the
+ * same contract as b200q_w4a16_gemm_peers (destinations, pads, ordering,
+ * timeouts) for b200q_mxfp8_gemm's operands, where B and scales_b hold this
+ * rank's N output columns.  No counterpart in the reference (single-GPU,
+ * generate_tasks.py:149); it replaces b200q_mxfp8_gemm + an all-gather. */
+int b200q_mxfp8_gemm_peers(const void* a, const void* scales_a, const void* b, const void* scales_b,
+                           void* const* y_peers, int n_peers, int64_t ldy, int64_t col0, void* const* pads, int rank,
+                           int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Barrier across the world ranks of one node, enqueued on `stream`.
  * pads[i] is rank i's signal pad (as above; the barrier uses words disjoint
  * from the GEMM's).  Orders this stream's earlier writes (peer stores
@@ -233,6 +243,12 @@ int b200q_w4a16_gemm_peers(const void* x, const int32_t* qweight, const void* sc
  * 10 s makes the wait give up and sets B200Q_DEV_ERR_TIMEOUT in the workspace
  * status word. */
 int b200q_peer_barrier(void* const* pads, int world, int rank, void* workspace, void* stream);
+
+/* Wait limit of b200q_peer_barrier in milliseconds (process-wide; <= 0
+ * restores the default 10 s).  Returns the previous limit.  Lets a test or a
+ * health check give up on a missing peer sooner.  No counterpart in the
+ * reference. */
+int64_t b200q_set_peer_barrier_timeout_ms(int64_t ms);
 
 #ifdef __cplusplus
 }

@@ -60,7 +60,10 @@ SIGNATURES = {
                                          _c_vp, _c_vp]),
     "b200q_lora_expand_add": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64,
                                              ctypes.c_int, _c_vp, _c_vp]),
+    "b200q_mxfp8_gemm_peers": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, ctypes.c_int, _c_i64, _c_i64,
+                                              _c_vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_vp, _c_sz, _c_vp]),
     "b200q_peer_barrier": (ctypes.c_int, [_c_vp, ctypes.c_int, ctypes.c_int, _c_vp, _c_vp]),
+    "b200q_set_peer_barrier_timeout_ms": (_c_i64, [_c_i64]),
 }
 
 _lock = threading.Lock()

@@ -132,11 +132,12 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* a) {
 
 // Waits until (int)(*a - target) >= 0 (wrap-safe epochs); false after
 // B200Q_PEER_WAIT_NS.
-__device__ __forceinline__ bool wait_epoch(const uint32_t* a, uint32_t target) {
+__device__ __forceinline__ bool wait_epoch(const uint32_t* a, uint32_t target,
+                                           uint64_t limit_ns = B200Q_PEER_WAIT_NS) {
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if ((int)(ld_acquire_sys(a) - target) >= 0) return true;
-    if ((it & 63) == 63 && globaltimer() - t0 > B200Q_PEER_WAIT_NS) return false;
+    if ((it & 63) == 63 && globaltimer() - t0 > limit_ns) return false;
     __nanosleep(32);
   }
 }

@@ -7,9 +7,9 @@
 //
 // Arithmetic.  Each weight enters the tensor core as the fp16 value
 // (1024 + nib) (1024 + 16 nib for odd nibble positions; 128 + nib in bf16),
-// formed from the packed word by one LOP3 (magic exponent, exact).  One more
-// MMA per 16 rows against a column of ones gives X[m] = sum_k x[m, k] over the
-// group, and the group is folded into the fp32 result as
+// formed from the packed word by one LOP3 (magic exponent, exact).  A
+// dedicated warp sums x over every group, X[m] = sum_k x[m, k], and the group
+// is folded into the fp32 result as
 //     y[m, n] += s' * acc[m, n] - s' * (1024 + z') * X[m]      (s' = s or s/16, z' = z or 16 z)
 // = s * sum_k x[m, k] (nib - z): the reference's fp32 ground truth
 // (kb_verifier.py:194-196 re-evaluates the module with w = (nib - z) * s in
@@ -18,33 +18,40 @@
 //
 // Design (HBM-bound: 31.8 MB per call at M=16, K=14336, N=4096):
 //  * The N axis is cut into 256-column strips (32 packed words = 128 B per K
-//    row); the K axis of each strip into `splits` contiguous ranges so that
-//    strips x splits ~= one CTA per SM (split-K).  M is cut into 16-row chunks
-//    (grid y).
-//  * One producer thread streams 128-row stages with TMA (128B-swizzled) into
-//    a 4-deep ring: the packed weight tile (16 KB), the x tile and the
-//    scale/zero rows of the stage.
+//    row); the K axis of each strip into `splits` contiguous ranges, and the
+//    K ranges of a strip form one thread-block cluster (up to 16 CTAs, one per
+//    SM, sized so that every cluster of the grid is resident at once).  M is
+//    cut into 16-row chunks (grid y).
+//  * One producer thread initialises the barriers and streams 128-row stages
+//    with TMA (128B-swizzled) into an 8-deep ring: the packed weight tile
+//    (16 KB), the x tile and the scale/zero rows of the stage.
 //  * 16 consumer warps.  Stage it goes to the 8 warps with parity it % 2;
 //    among those, warp (cg, th) owns packed-word columns [8cg, 8cg + 8) and
 //    nibble positions [4th, 4th + 4), i.e. 32 output columns, over all 128
 //    rows of the stage.  Thread (g, c) loads rows 2c, 2c+1, 2c+8, 2c+9 of word
 //    column 8cg + g (the standard m16n8k16 B fragment: one PRMT pairs a byte of
 //    two rows, one LOP3 per nibble position makes the f16x2 register).  A is
-//    the swizzled x tile, one ldmatrix.x4 per 16 rows.  All shared-memory
-//    offsets are per-thread constants plus compile-time immediates.
+//    the swizzled x tile, one ldmatrix.x4 per 16 rows.  Shared-memory loads
+//    are plain loads and the MMAs are not volatile, so the compiler can issue
+//    the next step's loads ahead of the current step's math.
+//  * One more warp sums x per group and row for every stage (fp32), so the
+//    legacy tensor pipe only does the useful products.
 //  * The fold's per-column factors (s', s' (1024 + z')) are computed once per
 //    warp, one column per lane, and shared through a small per-warp buffer.
-//  * Split-K partials go to caller workspace slots; the last CTA of a strip
-//    (atomic ticket, no spinning) sums the slots in a fixed order, writes y,
-//    clears the slots and resets its ticket: deterministic, workspace left
-//    zeroed.
+//  * Split-K: each CTA leaves its fp32 partial [16, 256] in shared memory; after
+//    a cluster barrier CTA r sums 16-byte chunks [r * 512 / S, (r+1) * 512 / S)
+//    of the strip over the S partials over DSMEM, in rank order
+//    (deterministic), and stores them.  No workspace beyond the status word.
 //  * Programmatic dependent launch (optional, b200q_set_weight_prefetch): the
 //    kernel lets the next kernel in the stream launch at once and streams the
 //    first ring of weight/scale/zero stages before `griddepcontrol.wait`;
-//    x is read, and y / the workspace written, only after the wait.  Legal only
-//    when the kernel just before this one in the stream does not write this
-//    call's qweight / scales / zeros (true for inference weights).
+//    x is read, and y written, only after the wait.  Legal only when the kernel
+//    just before this one in the stream does not write this call's qweight /
+//    scales / zeros (true for inference weights).
+#include <array>
+#include <mutex>
 #include <type_traits>
+#include <vector>
 
 #include "common.cuh"
 
@@ -55,10 +62,13 @@ constexpr int STRIP_WORDS = 32;
 constexpr int STRIP_COLS = STRIP_WORDS * 8;  // 256
 constexpr int KS = 128;                      // K rows per stage
 constexpr int NCONS = 16;                    // consumer warps
-constexpr int THREADS = (NCONS + 1) * 32;
-constexpr int STAGES = 4;
-constexpr int MAX_SPLITS = 32;     // split-K ranges per strip
-constexpr int HEADER_BYTES = 256;  // workspace: [status int | pad] then tickets then partials
+constexpr int XWARP = NCONS;                 // the x-sum warp
+constexpr int PWARP = NCONS + 1;             // the producer warp
+constexpr int THREADS = (NCONS + 2) * 32;
+constexpr int STAGES = 8;
+constexpr int MAX_CLUSTER = 16;
+constexpr int HEADER_BYTES = 256;  // workspace: [status int | pad]
+constexpr int PRS = STRIP_COLS + 8;  // row pitch (floats) of the CTA partial
 
 struct Layout {
   static constexpr int QW = KS * STRIP_WORDS * 4;  // 16 KB
@@ -67,53 +77,54 @@ struct Layout {
   static constexpr int SZ = 4 * STRIP_COLS * 2;  // up to 4 scale rows per stage (group 32)
   static constexpr int STAGE = QW + X + 2 * SZ;
   static constexpr int RING = STAGES * STAGE;
+  static constexpr int XS = STAGES * 4 * 16 * 4;  // x sums: [stage][group row][16 rows] fp32
   static constexpr int BARS = 256;
   static constexpr int FOLD = NCONS * 32 * 8;  // per-warp fold factors (float2 per lane)
-  static constexpr int SMEM = RING + BARS + FOLD + 1024 /*align*/;
-  static constexpr int N_INT = 16 * STRIP_COLS;  // fp32 outputs of a CTA
+  static constexpr int SMEM = RING + XS + BARS + FOLD + 1024 /*align*/;
   static_assert(STAGE % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
-  static_assert(2 * N_INT * 4 + 16 * STRIP_COLS * 2 <= RING, "reduction buffer and output tile must fit in the ring");
+  static_assert(16 * PRS * 4 <= RING, "the partial must fit in the ring");
 };
 
+// Not volatile: a pure register operation, so the compiler may schedule the
+// next step's shared-memory loads above it (software pipelining).
 __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1, bool bf16) {
   if (!bf16) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   }
 }
 
+// Ordered with the other memory operations ("memory"), not with the math.
 __device__ __forceinline__ void ldmatrix_x4(uint32_t* r, uint32_t saddr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(saddr));
+  asm("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(saddr)
+      : "memory");
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t saddr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
-  return v;
-}
-__device__ __forceinline__ uint16_t lds16(uint32_t saddr) {
-  uint16_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(saddr));
-  return v;
-}
 __device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(saddr));
   return v;
 }
-__device__ __forceinline__ void sts_f2(uint32_t saddr, float a, float b) {
-  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr), "f"(a), "f"(b) : "memory");
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ int ld_cluster_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -124,74 +135,78 @@ template <bool BF16, int FS>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-                        const __grid_constant__ OutSet out, int M, int N, int group, int strips, int splits,
-                        int n_stages_total, int prefetch, uint8_t* __restrict__ ws) {
+                        const __grid_constant__ OutSet out, int M, int N, int group, int splits,
+                        int n_stages_total, int prefetch, int* __restrict__ status) {
   using L = Layout;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int GPS = 8 / FS;  // groups (scale rows) per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::RING);
+  float* xs = reinterpret_cast<float*>(smem + L::RING);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::RING + L::XS);
   uint64_t* empty = full + STAGES;
-  __shared__ int s_last;
+  uint64_t* xready = empty + STAGES;
   __shared__ int s_err;
-
-  int* status = reinterpret_cast<int*>(ws);
+  __shared__ int s_any_err;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int strip = blockIdx.x / splits, split = blockIdx.x % splits;
+  const int strip = blockIdx.x / splits, split = blockIdx.x % splits;  // split == cluster rank
   const int mchunk = blockIdx.y;
   const int st0 = (int)((long long)split * n_stages_total / splits);
   const int st1 = (int)((long long)(split + 1) * n_stages_total / splits);
   const int nst = st1 - st0;
   const int srows = group >= KS ? 1 : KS / group;
   const uint32_t stage_bytes = L::QW + L::X + 2u * srows * STRIP_COLS * 2u;
-  int* tickets = reinterpret_cast<int*>(ws + HEADER_BYTES);
-  float* partials = reinterpret_cast<float*>(ws + HEADER_BYTES + (((size_t)gridDim.y * strips * 4 + 255) & ~size_t(255)));
 
-  if (prefetch && threadIdx.x == 0) pdl_trigger();
-  if (threadIdx.x == 0) {
+  // the producer thread initialises the barriers and starts the weight stream
+  // before the CTA barrier: every other warp waits on a barrier only after it
+  const bool producer = warp == PWARP && lane == 0;
+  auto load_w = [&](int it) {
+    uint8_t* st = smem + (it % STAGES) * L::STAGE;
+    const int k0 = (st0 + it) * KS;
+    uint64_t* bar = &full[it % STAGES];
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    tma_load_2d_hint(st, &tm_qw, strip * STRIP_WORDS, k0, bar, policy_evict_first());
+    tma_load_2d(st + L::QW + L::X, &tm_s, strip * STRIP_COLS, k0 / group, bar);
+    tma_load_2d(st + L::QW + L::X + L::SZ, &tm_z, strip * STRIP_COLS, k0 / group, bar);
+  };
+  auto load_x = [&](int it) {
+    uint8_t* st = smem + (it % STAGES) * L::STAGE;
+    const int k0 = (st0 + it) * KS;
+    uint64_t* bar = &full[it % STAGES];
+    tma_load_2d(st + L::QW, &tm_x, k0, mchunk * 16, bar);
+    tma_load_2d(st + L::QW + L::XBOX, &tm_x, k0 + 64, mchunk * 16, bar);
+  };
+  const int fill = nst < STAGES ? nst : STAGES;
+  if (producer) {
+    if (prefetch) pdl_trigger();
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCONS / 2);
+      mbar_init(&empty[s], NCONS / 2 + 1);
+      mbar_init(&xready[s], 1);
     }
     fence_barrier_init();
     s_err = 0;
     if (blockIdx.x == 0 && blockIdx.y == 0) peer_arrive(out);
-  }
-  if (warp == NCONS && lane == 0) {
-    prefetch_tmap(&tm_qw);
-    prefetch_tmap(&tm_x);
-    prefetch_tmap(&tm_s);
-    prefetch_tmap(&tm_z);
+    // ring fill: weights first (independent of the previous kernel), then
+    // the dependency wait, then activations
+    for (int it = 0; it < fill; ++it) load_w(it);
+    pdl_wait();
+    for (int it = 0; it < fill; ++it) load_x(it);
   }
   __syncthreads();
 
-  if (warp == NCONS) {
+  float tot[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) tot[u][r] = 0.f;
+  const int g = lane >> 2, c = lane & 3;
+  const int par = warp >> 3, cg = warp & 3, th = (warp >> 2) & 1;
+
+  if (warp == PWARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_stream = policy_evict_first();
-      auto load_w = [&](int it) {
-        uint8_t* st = smem + (it % STAGES) * L::STAGE;
-        const int k0 = (st0 + it) * KS;
-        uint64_t* bar = &full[it % STAGES];
-        mbar_arrive_expect_tx(bar, stage_bytes);
-        tma_load_2d_hint(st, &tm_qw, strip * STRIP_WORDS, k0, bar, pol_stream);
-        tma_load_2d(st + L::QW + L::X, &tm_s, strip * STRIP_COLS, k0 / group, bar);
-        tma_load_2d(st + L::QW + L::X + L::SZ, &tm_z, strip * STRIP_COLS, k0 / group, bar);
-      };
-      auto load_x = [&](int it) {
-        uint8_t* st = smem + (it % STAGES) * L::STAGE;
-        const int k0 = (st0 + it) * KS;
-        uint64_t* bar = &full[it % STAGES];
-        tma_load_2d(st + L::QW, &tm_x, k0, mchunk * 16, bar);
-        tma_load_2d(st + L::QW + L::XBOX, &tm_x, k0 + 64, mchunk * 16, bar);
-      };
-      // ring fill: weights first (independent of the previous kernel), then
-      // the dependency wait, then activations
-      const int fill = nst < STAGES ? nst : STAGES;
-      for (int it = 0; it < fill; ++it) load_w(it);
-      pdl_wait();
-      for (int it = 0; it < fill; ++it) load_x(it);
       int it = fill;
       for (; it < nst; ++it) {
         const int s = it % STAGES;
@@ -207,18 +222,56 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&full[j % STAGES], (j / STAGES) & 1, status);
     }
-  }
-
-  // ------------------------------------------------------------ consumers
-  const int g = lane >> 2, c = lane & 3;
-  const int par = warp >> 3, cg = warp & 3, th = (warp >> 2) & 1;
-  float tot[4][4];
+  } else if (warp == XWARP) {
+    // ------------------------------------------------------------ x sums per group row
+    // lane: row l % 16, k half l / 16 (box l / 16 of the stage's x tile);
+    // two partial sums of 32 k each (group 32 needs them apart)
+    const int row = lane & 15, hb = lane >> 4;
+    for (int it = 0; it < nst; ++it) {
+      const int s = it % STAGES;
+      if (!mbar_wait(&full[s], (it / STAGES) & 1, status)) {
+        atomicOr(&s_err, 1);
+        break;
+      }
+      const uint8_t* xb = smem + s * L::STAGE + L::QW + hb * L::XBOX + row * 128;
+      float h[2] = {0.f, 0.f};
 #pragma unroll
-  for (int u = 0; u < 4; ++u)
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xb + ((ch ^ (row & 7)) << 4));
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) tot[u][r] = 0.f;
-
-  if (warp < NCONS) {
+        for (int q = 0; q < 4; ++q) {
+          if (!BF16) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&vv[q]));
+            f[2 * q] = t.x;
+            f[2 * q + 1] = t.y;
+          } else {
+            f[2 * q] = __uint_as_float(vv[q] << 16);
+            f[2 * q + 1] = __uint_as_float(vv[q] & 0xFFFF0000u);
+          }
+        }
+        h[ch >> 2] += ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+      }
+      float* xo = xs + s * 64;
+      if (GPS == 1) {
+        const float tsum = h[0] + h[1];
+        const float other = __shfl_xor_sync(0xffffffffu, tsum, 16);
+        if (hb == 0) xo[row] = tsum + other;
+      } else if (GPS == 2) {
+        xo[hb * 16 + row] = h[0] + h[1];
+      } else {
+        xo[(2 * hb) * 16 + row] = h[0];
+        xo[(2 * hb + 1) * 16 + row] = h[1];
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&xready[s]);
+        mbar_arrive(&empty[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
     const int wcol = cg * 8 + g;  // word column whose weights this thread loads
     uint32_t woff[4], xoff[4];
 #pragma unroll
@@ -232,12 +285,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int q = 0; q < 4; ++q) xoff[q] = L::QW + R * 128 + (((2 * q + (mi >> 1)) ^ rr) << 4);
     }
     // fold factors: this lane computes column (word 8cg + lane/4, nibble 4th + lane%4)
-    const uint32_t fold_buf = smem_u32(smem + L::RING + L::BARS) + warp * 256;
+    float* fold_buf = reinterpret_cast<float*>(smem + L::RING + L::XS + L::BARS + warp * 256);
     const int fcol = (cg * 8 + (lane >> 2)) * 8 + 4 * th + (lane & 3);
     const bool fodd = (lane & 1) != 0;
     const uint32_t sel0 = (uint32_t)((2 * th) | ((2 * th) << 4) | ((4 + 2 * th) << 8) | ((4 + 2 * th) << 12));
     const uint32_t sel1 = sel0 + 0x1111u;
-    const uint32_t one2 = BF16 ? 0x3F803F80u : 0x3C003C00u;
     const uint32_t magic = BF16 ? 0x43004300u : 0x64006400u;
 
     for (int it = par; it < nst; it += 2) {
@@ -246,10 +298,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         atomicOr(&s_err, 1);
         break;
       }
-      const uint32_t st = smem_u32(smem + s * L::STAGE);
+      const uint8_t* stp = smem + s * L::STAGE;
+      const uint32_t st = smem_u32(stp);
 #pragma unroll
-      for (int f = 0; f < 8 / FS; ++f) {
-        float acc[4][4], ax[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int f = 0; f < GPS; ++f) {
+        float acc[4][4];
 #pragma unroll
         for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -259,9 +312,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int ks = f * FS + j;
           uint32_t w[4], a[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) w[i] = lds32(st + ks * 2048 + woff[i]);
+          for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(stp + ks * 2048 + woff[i]);
           ldmatrix_x4(a, st + (ks >> 2) * L::XBOX + xoff[ks & 3]);
-          mma_16816(ax, a, one2, one2, BF16);
 #pragma unroll
           for (int bb = 0; bb < 2; ++bb) {
             const uint32_t sel = bb ? sel1 : sel0;
@@ -283,8 +335,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // fold this group into tot
         {
           const int srow = group >= KS ? 0 : f;
-          const uint32_t so = st + L::QW + L::X + srow * (STRIP_COLS * 2) + fcol * 2;
-          const uint16_t sb = lds16(so), zb = lds16(so + L::SZ);
+          const uint8_t* so = stp + L::QW + L::X + srow * (STRIP_COLS * 2) + fcol * 2;
+          const uint16_t sb = *reinterpret_cast<const uint16_t*>(so);
+          const uint16_t zb = *reinterpret_cast<const uint16_t*>(so + L::SZ);
           float sf, zz;
           if (!BF16) {
             sf = __half2float(__ushort_as_half(sb));
@@ -298,13 +351,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             sf = __uint_as_float((uint32_t)sb << 16);
             zz = __uint_as_float((uint32_t)zb << 16) + 128.f;
           }
-          sts_f2(fold_buf + lane * 8, sf, sf * zz);
+          reinterpret_cast<float2*>(fold_buf)[lane] = make_float2(sf, sf * zz);
+          if (f == 0 && !mbar_wait(&xready[s], (it / STAGES) & 1, status)) atomicOr(&s_err, 1);
           __syncwarp();
+          const float x0 = xs[s * 64 + f * 16 + g];
+          const float x1 = xs[s * 64 + f * 16 + g + 8];
           // entries 8c .. 8c+7: (word 2c, nibbles 4th..4th+3), (word 2c+1, same)
           float fa[16];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const float4 v = lds_f4(fold_buf + c * 64 + q * 16);
+            const float4 v = reinterpret_cast<const float4*>(fold_buf)[c * 4 + q];
             fa[4 * q] = v.x;
             fa[4 * q + 1] = v.y;
             fa[4 * q + 2] = v.z;
@@ -317,7 +373,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int r = 0; r < 4; ++r) {
               const int e = (r & 1) * 4 + u;  // entry within the thread's 8
               tot[u][r] = fmaf(fa[2 * e], acc[u][r], tot[u][r]);
-              tot[u][r] = fmaf(-fa[2 * e + 1], ax[(r >> 1) * 2], tot[u][r]);
+              tot[u][r] = fmaf(-fa[2 * e + 1], (r >> 1) ? x1 : x0, tot[u][r]);
             }
         }
       }
@@ -327,113 +383,91 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   __syncthreads();
-  pdl_wait();  // y and the workspace may still be in use by the previous kernel
-  do {
-    if (s_err) break;  // status word already records the timeout
+  pdl_wait();  // y may still be in use by the previous kernel
 
-    // ---------------------------------------------------------------- CTA reduction over the two stage parities
-    // Internal order i = ((cg * 2 + th) * 16 + u * 4 + r) * 32 + lane: the
-    // smem writes and reads are lane-contiguous (conflict-free); workspace
-    // slots use the same order; only the final store maps i to (row, column).
-    float* red = reinterpret_cast<float*>(smem);
-    if (warp < NCONS) {
+  // -------------------------------------------------------------------- epilogue
+  // 1. this CTA's partial [16, 256] fp32 (sum of the two stage parities) in
+  //    shared memory at the start of the (now idle) ring: part[row * PRS +
+  //    word * 8 + nibble]; a thread's (row, word) holds 4 consecutive nibbles,
+  //    one float4, and the padded row pitch halves the store conflicts;
+  // 2. cluster barrier; CTA r sums its chunks over the cluster's partials in
+  //    rank order and stores them; 3. cluster barrier (partials stay readable).
+  float* part = reinterpret_cast<float*>(smem);
+  if (warp < NCONS) {
+    float4* dst[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+    for (int r = 0; r < 4; ++r)
+      dst[r] = reinterpret_cast<float4*>(part + (g + 8 * (r >> 1)) * PRS + (cg * 8 + 2 * c + (r & 1)) * 8 + 4 * th);
+    if (par == 1) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) red[par * L::N_INT + (((cg * 2 + th) * 16 + u * 4 + r) << 5) + lane] = tot[u][r];
+      for (int r = 0; r < 4; ++r) *dst[r] = make_float4(tot[0][r], tot[1][r], tot[2][r], tot[3][r]);
     }
-    __syncthreads();
-
-    const int rows_here = min(16, M - mchunk * 16);
-    const int n_int = L::N_INT;
-    const size_t strip_id = (size_t)mchunk * strips + strip;
-    float* my_slot = partials + (strip_id * splits + split) * (size_t)n_int;
-    const int tid = threadIdx.x;
-    auto row_of = [](int i) { return ((i & 31) >> 2) + (((i >> 5) & 3) >> 1) * 8; };
-    auto col_of = [](int i) {  // column within the 256-column strip
-      const int ln = i & 31, e = (i >> 5) & 15, q = i >> 9;
-      return 8 * ((q >> 1) * 8 + 2 * (ln & 3) + (e & 1)) + 4 * (q & 1) + (e >> 2);
-    };
-    // the output block is assembled in shared memory (after the reduction
-    // buffer) and leaves as whole rows of 16-byte chunks: coalesced in HBM and
-    // few, large writes when the destinations are peers over NVLink
-    T* tile = reinterpret_cast<T*>(smem + 2 * n_int * 4);
-    auto write_rows = [&]() {
-      for (int e = tid; e < rows_here * (STRIP_COLS / 8); e += THREADS) {
-        const int row = e / (STRIP_COLS / 8), ch = e % (STRIP_COLS / 8);
-        const int gcol = strip * STRIP_COLS + ch * 8;
-        if (gcol >= N) continue;  // N % 32 == 0: a chunk is wholly inside or outside
-        const uint4 v = *reinterpret_cast<const uint4*>(tile + row * STRIP_COLS + ch * 8);
-        for (int o = 0; o < out.n; ++o)
-          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(out.y[o]) + (size_t)(mchunk * 16 + row) * out.ldy +
-                                    out.col0 + gcol) = v;
+    named_barrier_sync(1, NCONS * 32);
+    if (par == 0) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float4 o = *dst[r];
+        *dst[r] = make_float4(o.x + tot[0][r], o.y + tot[1][r], o.z + tot[2][r], o.w + tot[3][r]);
       }
-    };
-    if (splits == 1 && out.world > 1) {
-      if (tid == 0 && !peer_wait_arrivals(out, status)) s_err = 1;
-      __syncthreads();
-      if (s_err) break;
     }
-    for (int i = tid; i < n_int; i += THREADS) {
-      const int row = row_of(i);
-      if (row >= rows_here) continue;
-      const float v = red[i] + red[n_int + i];
-      if (splits == 1)
-        tile[row * STRIP_COLS + col_of(i)] = (T)v;
-      else
-        my_slot[i] = v;
-    }
-    if (splits == 1) {
-      __syncthreads();
-      write_rows();
-      break;
-    }
+  }
+  if (threadIdx.x == 0) s_any_err = s_err;
+  if (splits > 1) cluster_sync(); else __syncthreads();
 
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&tickets[strip_id], 1) == splits - 1);
-    __syncthreads();
-    if (!s_last) break;
-    __threadfence();
-    if (out.world > 1) {
-      if (tid == 0 && !peer_wait_arrivals(out, status)) s_err = 1;
-      __syncthreads();
-      if (s_err) break;
-    }
-    // slots are read in batches of 8 independent L2 loads per thread and
-    // added in slot order, so the result does not depend on which CTA
-    // finished last.  The slots are cleared after reading: every workspace
-    // byte this kernel wrote goes back to zero.
-    float4* slots = reinterpret_cast<float4*>(partials + strip_id * splits * (size_t)n_int);
-    const int slot4 = n_int / 4;
-    for (int i4 = tid; i4 < slot4; i4 += THREADS) {
-      const int i = i4 * 4;
-      const int row = row_of(i);  // the 4 lanes of a float4 share a row
-      if (row >= rows_here) continue;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp0 = 0; sp0 < splits; sp0 += 8) {
-        float4 part[8];
+  const int rows_here = min(16, M - mchunk * 16);
+  const int tid = threadIdx.x;
+  // any CTA of the cluster that gave up a wait leaves its partial incomplete:
+  // then nobody in the cluster stores
+  if (splits > 1 && tid < splits) {
+    const int e = ld_cluster_s32(map_shared_rank(smem_u32(&s_any_err), (uint32_t)tid));
+    if (e) atomicOr(&s_err, 1);
+  }
+  if (out.world > 1 && tid == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
+  __syncthreads();
+  if (s_err == 0) {
+    // chunks of 8 columns, row-major over the strip: [16 rows x 32 chunks]
+    const int c0 = split * 512 / splits, c1 = (split + 1) * 512 / splits;
+    for (int ch = c0 + tid; ch < c1; ch += THREADS) {
+      const int row = ch >> 5, cc = ch & 31;
+      const int gcol = strip * STRIP_COLS + cc * 8;
+      if (row >= rows_here || gcol >= N) continue;  // N % 32 == 0: a chunk is wholly inside or outside
+      const uint32_t off = smem_u32(part + row * PRS + cc * 8);
+      float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+      // peers' partials in batches of 4 (8 DSMEM loads in flight), summed in rank order
+      for (int p0 = 0; p0 < splits; p0 += 4) {
+        float4 a0[4], a1[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (sp0 + j < splits) part[j] = __ldcg(slots + (sp0 + j) * slot4 + i4);
+        for (int j = 0; j < 4; ++j)
+          if (p0 + j < splits) {
+            const uint32_t a = splits > 1 ? map_shared_rank(off, (uint32_t)(p0 + j)) : off;
+            a0[j] = splits > 1 ? ld_cluster_f4(a) : lds_f4(a);
+            a1[j] = splits > 1 ? ld_cluster_f4(a + 16) : lds_f4(a + 16);
+          }
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (sp0 + j < splits) {
-            __stcg(slots + (sp0 + j) * slot4 + i4, make_float4(0.f, 0.f, 0.f, 0.f));
-            v.x += part[j].x;
-            v.y += part[j].y;
-            v.z += part[j].z;
-            v.w += part[j].w;
+        for (int j = 0; j < 4; ++j)
+          if (p0 + j < splits) {
+            v0.x += a0[j].x, v0.y += a0[j].y, v0.z += a0[j].z, v0.w += a0[j].w;
+            v1.x += a1[j].x, v1.y += a1[j].y, v1.z += a1[j].z, v1.w += a1[j].w;
           }
       }
-      const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tile[row * STRIP_COLS + col_of(i + q)] = (T)vv[q];
+      uint4 o;
+      if (!BF16) {
+        __half2 h0 = __floats2half2_rn(v0.x, v0.y), h1 = __floats2half2_rn(v0.z, v0.w);
+        __half2 h2 = __floats2half2_rn(v1.x, v1.y), h3 = __floats2half2_rn(v1.z, v1.w);
+        o = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+      } else {
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v0.x, v0.y), h1 = __floats2bfloat162_rn(v0.z, v0.w);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v1.x, v1.y), h3 = __floats2bfloat162_rn(v1.z, v1.w);
+        o = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+      }
+      for (int d = 0; d < out.n; ++d)
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(out.y[d]) + (size_t)(mchunk * 16 + row) * out.ldy + out.col0 +
+                                  gcol) = o;
     }
-    __syncthreads();
-    write_rows();
-    if (tid == 0) tickets[strip_id] = 0;  // leave the workspace zeroed for the next call
-  } while (0);
+  }
+  if (splits > 1) cluster_sync();  // no CTA exits while its partial may still be read
   if (out.world > 1) {
     __syncthreads();
     if (threadIdx.x < 32) peer_finish(out, status);
@@ -442,7 +476,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 struct Plan {
   int mchunks, strips, splits, n_stages;
-  size_t ws_bytes;
 };
 
 Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
@@ -454,21 +487,57 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   int sp = sms / (p.strips * p.mchunks);
   if (sp < 1) sp = 1;
   if (sp > p.n_stages) sp = p.n_stages;
-  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
+  if (sp > MAX_CLUSTER) sp = MAX_CLUSTER;
   p.splits = sp;
-  const size_t tickets = ((size_t)p.mchunks * p.strips * 4 + 255) & ~size_t(255);
-  const size_t parts = p.splits > 1 ? (size_t)p.mchunks * p.strips * p.splits * Layout::N_INT * sizeof(float) : 0;
-  p.ws_bytes = HEADER_BYTES + tickets + parts;
   return p;
 }
 
+// Largest cluster size <= want whose clusters (n_clusters of them) are all
+// resident at once; cached per (device, kernel, n_clusters, want).
+template <class Kern>
+static int fit_cluster(Kern kern, int want, int n_clusters) {
+  static std::mutex mu;
+  static std::vector<std::array<long long, 5>> cache;  // device, kernel, n_clusters, want, result
+  const int dev = current_device();
+  const long long kid = (long long)reinterpret_cast<uintptr_t>(reinterpret_cast<const void*>(kern));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& e : cache)
+      if (e[0] == dev && e[1] == kid && e[2] == n_clusters && e[3] == want) return (int)e[4];
+  }
+  int cs = want;
+  for (; cs > 1; --cs) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(cs * n_clusters);
+    q.blockDim = dim3(THREADS);
+    q.dynamicSmemBytes = Layout::SMEM;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = (unsigned)cs;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, kern, &q) == cudaSuccess && active >= n_clusters) break;
+    cudaGetLastError();  // a refused size is not an error of this call
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache.push_back({dev, kid, n_clusters, want, cs});
+  return cs;
+}
+
 template <bool BF16, int FS>
-static int launch_t(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s,
-                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, uint8_t* ws,
-                    cudaStream_t stream) {
+static int launch_t(Plan p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s, const CUtensorMap& z,
+                    const OutSet& y, int M, int N, int group, int* status, cudaStream_t stream) {
   auto kern = w4a16_decode_kernel<BF16, FS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::SMEM);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(decode)");
+  if (p.splits > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(decode, non-portable cluster)");
+  }
+  if (p.splits > 1) p.splits = fit_cluster(kern, p.splits, p.strips * p.mchunks);
   // weight prefetch across the launch boundary only for single-GPU outputs:
   // the peer-store variant orders itself through its signal pads
   const int prefetch = (weight_prefetch_enabled() && y.world <= 1) ? 1 : 0;
@@ -477,38 +546,46 @@ static int launch_t(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, 
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = Layout::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (p.splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (prefetch) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = prefetch ? 1 : 0;
-  e = cudaLaunchKernelEx(&cfg, kern, qw, x, s, z, y, M, N, group, p.strips, p.splits, p.n_stages, prefetch, ws);
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kern, qw, x, s, z, y, M, N, group, p.splits, p.n_stages, prefetch, status);
   if (e != cudaSuccess) return check_cuda(e, "w4a16 decode launch");
   return check_cuda(cudaGetLastError(), "w4a16 decode launch");
 }
 
 template <bool BF16>
 static int launch_g(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s,
-                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, uint8_t* ws,
-                    cudaStream_t stream) {
-  if (group == 32) return launch_t<BF16, 2>(p, qw, x, s, z, y, M, N, group, ws, stream);
-  if (group == 64) return launch_t<BF16, 4>(p, qw, x, s, z, y, M, N, group, ws, stream);
-  return launch_t<BF16, 8>(p, qw, x, s, z, y, M, N, group, ws, stream);
+                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, int* status, cudaStream_t stream) {
+  if (group == 32) return launch_t<BF16, 2>(p, qw, x, s, z, y, M, N, group, status, stream);
+  if (group == 64) return launch_t<BF16, 4>(p, qw, x, s, z, y, M, N, group, status, stream);
+  return launch_t<BF16, 8>(p, qw, x, s, z, y, M, N, group, status, stream);
 }
 
 }  // namespace decode
 
-size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
-  return decode::plan(M, N, K, num_sms(device)).ws_bytes;
-}
+size_t w4a16_decode_ws_bytes(int64_t, int64_t, int64_t, int) { return decode::HEADER_BYTES; }
 
 int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream) {
   using namespace decode;
   const Plan p = plan(M, N, K, num_sms(-1));
-  if (!workspace || workspace_bytes < p.ws_bytes)
-    return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(p.ws_bytes) + " bytes required");
+  if (!workspace || workspace_bytes < (size_t)HEADER_BYTES)
+    return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(HEADER_BYTES) + " bytes required");
   if (group != 32 && group != 64 && group != 128 && group != 256)
     return fail(B200Q_ERR_UNSUPPORTED, "w4a16 decode: group must be 32, 64, 128 or 256");
   const CUtensorMapDataType h16 = CU_TENSOR_MAP_DATA_TYPE_UINT16;
@@ -525,9 +602,10 @@ int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, cons
   if ((rc = encode_2d(&tz, h16, zeros, N, K / group, (uint64_t)N * 2, STRIP_COLS, srows,
                       CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  if (dtype == B200Q_DTYPE_BF16) return launch_g<true>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, ws, stream);
-  return launch_g<false>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, ws, stream);
+  int* status = reinterpret_cast<int*>(workspace);
+  if (dtype == B200Q_DTYPE_BF16)
+    return launch_g<true>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, status, stream);
+  return launch_g<false>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, status, stream);
 }
 
 }  // namespace b200q

@@ -9,6 +9,7 @@ tensor is an error."""
 from __future__ import annotations
 
 import threading
+from typing import Optional
 
 import torch
 
@@ -171,6 +172,7 @@ def _(x_int8, w_int8, x_scale, w_scale):
     return x_int8.new_empty((x_int8.shape[0], w_int8.shape[1]), dtype=torch.float16)
 
 
+@torch.library.custom_op("b200q::mxfp8_gemm", mutates_args=())
 def mxfp8_gemm(a: torch.Tensor, scales_a: torch.Tensor, b: torch.Tensor, scales_b: torch.Tensor) -> torch.Tensor:
     """y[M, N] = fp16(A_deq . B_deq^T) for OCP-MX e4m3 operands (codes as uint8 or
     float8_e4m3fn [M, K] / [N, K], E8M0 scales uint8 [M, K/32] / [N, K/32])."""
@@ -192,7 +194,37 @@ def mxfp8_gemm(a: torch.Tensor, scales_a: torch.Tensor, b: torch.Tensor, scales_
     return y
 
 
-def moe_route(router_logits: torch.Tensor):
+@mxfp8_gemm.register_fake
+def _(a, scales_a, b, scales_b):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.float16)
+
+
+def mxfp8_gemm_peers(a: torch.Tensor, scales_a: torch.Tensor, b: torch.Tensor, scales_b: torch.Tensor,
+                     y_ptrs, ldy: int, col0: int, pad_ptrs=None, rank: int = 0) -> None:
+    """Columns [col0, col0 + N) of y = A . B^T from this rank's B shard [N, K],
+    stored into every buffer of ``y_ptrs`` ([M, ldy] fp16, peers' included),
+    ordered against the peers through ``pad_ptrs`` as in w4a16_gemm_peers."""
+    if not a.is_cuda:
+        raise RuntimeError("mxfp8_gemm_peers runs on CUDA tensors only (no CPU implementation)")
+    a, b = (t.view(torch.uint8) if t.dtype != torch.uint8 else t for t in (a, b))
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K or scales_a.shape != (M, K // 32) or scales_b.shape != (N, K // 32):
+        raise ValueError("mxfp8_gemm_peers: shapes must be A [M,K], B [N,K], scales [*, K/32]")
+    a, b, scales_a, scales_b = (_aligned(t) for t in (a, b, scales_a, scales_b))
+    if M == 0:
+        return
+    L = _lib.lib()
+    ws = workspace(a.device, L.b200q_mxfp8_workspace_bytes(M, N, K, a.device.index))
+    pads = _ptr_array(pad_ptrs) if pad_ptrs is not None else None
+    _lib.check(L.b200q_mxfp8_gemm_peers(a.data_ptr(), scales_a.data_ptr(), b.data_ptr(), scales_b.data_ptr(),
+                                        _ptr_array(y_ptrs), len(y_ptrs), ldy, col0, pads, rank, M, N, K,
+                                        ws.data_ptr(), ws.numel(), _stream_ptr(a.device)))
+
+
+@torch.library.custom_op("b200q::moe_route", mutates_args=())
+def moe_route(router_logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                     torch.Tensor]:
     """Top-2 routing + expert-grouped permutation (see include/b200q.h).
     Returns topi [T,2] int32, gates [T,2] (logits dtype), offsets [E+1] int32,
     slot_token [2T] int32, token_slot [T,2] int32."""
@@ -212,13 +244,33 @@ def moe_route(router_logits: torch.Tensor):
     return topi, gates, offsets, slot_token, token_slot
 
 
+@moe_route.register_fake
+def _(router_logits):
+    T, E = router_logits.shape
+    i32 = dict(dtype=torch.int32)
+    return (router_logits.new_empty((T, 2), **i32), router_logits.new_empty((T, 2)),
+            router_logits.new_empty((E + 1,), **i32), router_logits.new_empty((2 * T,), **i32),
+            router_logits.new_empty((T, 2), **i32))
+
+
 def moe_grouped_gemm(x: torch.Tensor, offsets: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
                      zeros: torch.Tensor, group: int, up=None) -> torch.Tensor:
+    """See moe_grouped_gemm_op; ``up`` = (qweight_up, scales_up, zeros_up) or None."""
+    u = up if up is not None else (None, None, None)
+    return moe_grouped_gemm_op(x, offsets, qweight, scales, zeros, group, u[0], u[1], u[2])
+
+
+@torch.library.custom_op("b200q::moe_grouped_gemm", mutates_args=())
+def moe_grouped_gemm_op(x: torch.Tensor, offsets: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                        zeros: torch.Tensor, group: int, qweight_up: Optional[torch.Tensor] = None,
+                        scales_up: Optional[torch.Tensor] = None,
+                        zeros_up: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One launch over all experts.  x [rows, K] grouped by expert (rows of
     expert e at [offsets[e], offsets[e+1]), offsets on the device); qweight
     [E, K, N/8], scales / zeros [E, K/group, N].  Returns y [rows, N] =
     x . W_e, or with ``up = (qweight_up, scales_up, zeros_up)`` the fused
     SiLU(x . Wg_e) * (x . Wu_e)."""
+    up = None if qweight_up is None else (qweight_up, scales_up, zeros_up)
     if not x.is_cuda:
         raise RuntimeError("b200q moe_grouped_gemm runs on CUDA tensors only")
     rows, K = x.shape
@@ -243,6 +295,11 @@ def moe_grouped_gemm(x: torch.Tensor, offsets: torch.Tensor, qweight: torch.Tens
                                                  y.data_ptr(), rows, N, K, group, dt, ws.data_ptr(), ws.numel(),
                                                  _stream_ptr(x.device)))
     return y
+
+
+@moe_grouped_gemm_op.register_fake
+def _(x, offsets, qweight, scales, zeros, group, qweight_up=None, scales_up=None, zeros_up=None):
+    return x.new_empty((x.shape[0], qweight.shape[2] * 8))
 
 
 def pack_int4(codes: torch.Tensor, offset: int = 0) -> torch.Tensor:

@@ -158,6 +158,34 @@ class PeerGatherW4A16(nn.Module):
         return y
 
 
+class PeerGatherMXFP8(nn.Module):
+    """Column-sharded MXFP8 linear (B [N, K] split along N) whose all-gather is
+    fused into the GEMM epilogue, like PeerGatherW4A16: one kernel per rank
+    stores this rank's columns into every rank's y [M, N] fp16 over NVLink.
+    Returns a view of this module's peer-mapped buffer, valid until the next
+    forward call."""
+
+    def __init__(self, process_group: Optional[dist.ProcessGroup] = None):
+        super().__init__()
+        self.pg = process_group
+        self._bufs: Optional[PeerBuffers] = None
+
+    def forward(self, a: torch.Tensor, scales_a: torch.Tensor, b_shard: torch.Tensor,
+                scales_b_shard: torch.Tensor) -> torch.Tensor:
+        from . import ops
+        world = dist.get_world_size(self.pg)
+        rank = dist.get_rank(self.pg)
+        M = a.shape[0]
+        n = b_shard.shape[0]
+        N = n * world
+        if self._bufs is None:
+            self._bufs = PeerBuffers(a.device, self.pg)
+        buf, ptrs = self._bufs.output(M * N * 2)
+        y = buf[:M * N * 2].view(torch.float16).view(M, N)
+        ops.mxfp8_gemm_peers(a, scales_a, b_shard, scales_b_shard, ptrs, N, rank * n, self._bufs.pad_ptrs, rank)
+        return y
+
+
 def _grouped_experts_at(xs: torch.Tensor, offsets: torch.Tensor, w) -> torch.Tensor:
     """Grouped gate/up (fused SiLU * mul) and down GEMMs over rows already
     grouped by local expert (expert e at [offsets[e], offsets[e+1]); rows past

@@ -13,7 +13,8 @@ w4a16      numpy restatement of QUANT_REF (generate_tasks.py:45-74): packer,
            bit-exact unpack, fp16 dequant in the reference's op order, fp32
            ground truth (common/kb_verifier.py:194-196 convention).
 w8a8       numpy restatement of W8A8_REF (generate_tasks.py:198-215) plus the
-           SmoothQuant input preparation that BASELINE's config 2 describes.
+           the benchmark's SmoothQuant input preparation (alpha = 0.5 smoothing,
+           1 % outlier channels, per-token int8 activations).
 mxfp8      OCP-MX v1.0 e4m3 + E8M0 block quantiser and block-scaled GEMM; there
            is no reference module for this config (parity: see its header).
 moe        routing of MOE_REF / FUSED_QMOE_REF (generate_tasks.py:171-178,
@@ -21,9 +22,8 @@ moe        routing of MOE_REF / FUSED_QMOE_REF (generate_tasks.py:171-178,
 reference_port
            torch-CPU restatement of the reference ``Model.forward`` op sequence,
            used only as the timed CPU baseline.
-c/oracle.c C restatement of the integer parts (unpack, top-2 routing) and an
-           fp64 W4A16 GEMM, compiled by ``oracle/build.py`` into
-           ``oracle/_ref/liboracle.so`` and cross-checked against numpy.
+lora, silu_fp8
+           numpy restatements of LORA_REF / multi_lora_qgemm and FUSED_SILU_REF.
 
 Parity pinning: the numpy restatements are checked against golden vectors
 produced by the reference modules themselves (``tests/golden/make_golden.py``

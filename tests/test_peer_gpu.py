@@ -58,14 +58,20 @@ def test_peer_entry_argument_errors():
 
 def test_barrier_timeout_sets_status():
     """Rank 0 of a 2-rank barrier whose peer never signals: the wait ends
-    after its limit (10 s) with B200Q_DEV_ERR_TIMEOUT, and the context stays
-    usable.  Both 'pads' are local buffers; nothing faults or hangs."""
-    from kernelbench_harbor_b200 import ops
+    after its limit (shortened to 300 ms for the test) with
+    B200Q_DEV_ERR_TIMEOUT, and the context stays usable.  Both 'pads' are
+    local buffers; nothing faults or hangs."""
+    from kernelbench_harbor_b200 import _lib, ops
+    L = _lib.lib()
     mine = torch.zeros(64, dtype=torch.int32, device="cuda")
     peer = torch.zeros(64, dtype=torch.int32, device="cuda")
     ops.device_status()  # clear
-    ops.peer_barrier([mine.data_ptr(), peer.data_ptr()], 0, torch.device("cuda", 0))
-    torch.cuda.synchronize()
+    old = L.b200q_set_peer_barrier_timeout_ms(300)
+    try:
+        ops.peer_barrier([mine.data_ptr(), peer.data_ptr()], 0, torch.device("cuda", 0))
+        torch.cuda.synchronize()
+    finally:
+        L.b200q_set_peer_barrier_timeout_ms(old)
     assert int(peer[16]) == 1 and int(mine[61]) == 1  # our epoch was published
     assert ops.device_status() & 1
     # the context still runs kernels
@@ -120,3 +126,65 @@ def test_two_gpu_fused_gather():
     for rank, msg, worst in res:
         assert msg == "ok", f"rank {rank}: {msg}"
         assert worst < 2e-2
+
+
+def test_mxfp8_peer_entry_single_gpu_offsets():
+    from kernelbench_harbor_b200 import ops
+    from tests.test_mxfp8 import _inputs
+    for M in (128, 256):
+        ac, asc, bc, bsc = (t.cuda() for t in _inputs(M, 512, 1024, seed=3 + M))
+        ref = ops.mxfp8_gemm(ac, asc, bc, bsc)
+        ya = torch.full((M, 1536), 7.0, dtype=torch.float16, device="cuda")
+        yb = torch.full((M, 1536), -3.0, dtype=torch.float16, device="cuda")
+        ops.mxfp8_gemm_peers(ac, asc, bc, bsc, [ya.data_ptr(), yb.data_ptr()], 1536, 512)
+        torch.cuda.synchronize()
+        for y in (ya, yb):
+            assert torch.equal(y[:, 512:1024], ref)
+            assert torch.all(y[:, :512] == 7.0 if y is ya else y[:, :512] == -3.0)
+    assert ops.device_status() == 0
+
+
+def _mxfp8_worker(rank, world, port, q_out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from kernelbench_harbor_b200 import ops, parallel
+        from tests.test_mxfp8 import _inputs
+        mod = parallel.PeerGatherMXFP8()
+        for M, N in ((128, 1024), (512, 2048), (128, 1024)):
+            ac, asc, bc, bsc = (t.cuda() for t in _inputs(M, N, 2048, seed=5 + M))
+            n = N // world
+            expect = torch.cat([ops.mxfp8_gemm(ac, asc, bc[r * n:(r + 1) * n].contiguous(),
+                                               bsc[r * n:(r + 1) * n].contiguous()) for r in range(world)], dim=1)
+            mine = (bc[rank * n:(rank + 1) * n].contiguous(), bsc[rank * n:(rank + 1) * n].contiguous())
+            for _ in range(3):
+                y = mod(ac, asc, *mine)
+            torch.cuda.synchronize()
+            if not torch.equal(y, expect):
+                raise AssertionError(f"rank {rank} M={M}: fused gather differs from per-shard GEMMs")
+        if ops.device_status() != 0:
+            raise AssertionError("device status set")
+        q_out.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q_out.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_mxfp8_fused_gather():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mxfp8_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q_out.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, msg in res:
+        assert msg == "ok", f"rank {rank}: {msg}"

@@ -104,7 +104,7 @@ def test_reference_task_grid(ops, K, N, group, dtype):
 
 
 def test_benchmark_decode_config_vs_oracle(ops):
-    """M=16, K=14336, N=4096, g128, against the numpy oracle."""
+    """The benchmark's decode configuration: M=16, K=14336, N=4096, g128, against the numpy oracle."""
     x, q, s, z = w4a16_inputs(16, 14336, 4096, 128, "fp16", seed=1016, device="cuda")
     y = _run(ops, x, q, s, z, 128).float().cpu().numpy()
     ref = o.forward_fp32(x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy(), z.cpu().numpy(), 128)
@@ -139,12 +139,12 @@ def test_module_dropin(ops):
 
 
 @pytest.mark.parametrize("M,K,N,group,dtype", [
-    (128, 14336, 4096, 128, "fp16"),   # benchmark config 1 (split-K tiles)
+    (128, 14336, 4096, 128, "fp16"),   # the benchmark's M=128 sweep point (split-K tiles)
     (256, 1024, 512, 128, "fp16"),
     (300, 2048, 768, 64, "fp16"),      # ragged M tile, ragged N tile (768 = 3 x 256)
     (129, 4096, 1024, 32, "bf16"),
     (512, 4096, 1024, 256, "bf16"),
-    (1024, 14336, 4096, 128, "fp16"),  # benchmark config 1
+    (1024, 14336, 4096, 128, "fp16"),  # the benchmark's M=1024 sweep point
 ])
 def test_tensor_core_path(ops, M, K, N, group, dtype):
     x, q, s, z = w4a16_inputs(M, K, N, group, dtype, seed=M + K, device="cuda")
@@ -173,7 +173,7 @@ def test_split_256_row_tiles(ops, M, K, N, group, dtype):
 
 
 def test_tensor_core_full_config(ops):
-    """BASELINE config 1 at M=4096 against the fp32 torch reference."""
+    """The benchmark's compute-bound configuration, M=4096, against the fp32 torch reference."""
     x, q, s, z = w4a16_inputs(4096, 14336, 4096, 128, "fp16", seed=4096, device="cuda")
     y = _run(ops, x, q, s, z, 128)
     torch.testing.assert_close(y.float(), torch_ref_fp32(x, q, s, z, 128), **TOL)

@@ -59,9 +59,9 @@ def test_noalloc_rejects_oversize():
     p = dev.data_ptr()
     assert L.b200q_w4a16_gemm_noalloc(p, p, p, p, p, 64, 4096, 4096, 128, 0, None) == _lib.ERR_SHAPE
     assert b"M must be" in L.b200q_last_error()
-    # scratch need beyond the fixed array (many strips x splits)
-    assert L.b200q_w4a16_gemm_noalloc(p, p, p, p, p, 32, 1 << 30, 4096, 128, 0, None) == _lib.ERR_SHAPE
-    assert b"scratch" in L.b200q_last_error()
+    # N beyond the supported range
+    assert L.b200q_w4a16_gemm_noalloc(p, p, p, p, p, 32, (1 << 30) + 32, 4096, 128, 0, None) == _lib.ERR_SHAPE
+    assert b"too large" in L.b200q_last_error()
     # K beyond the 32-bit range the kernels index with
     assert L.b200q_w4a16_gemm_noalloc(p, p, p, p, p, 16, 4096, 1 << 31, 128, 0, None) == _lib.ERR_SHAPE
     assert b"too large" in L.b200q_last_error()
