@@ -104,6 +104,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared-memory base rounded up to 1024 bytes by pointer
+// arithmetic on the __shared__ array itself (not through an integer), so the
+// compiler still knows the result points into shared memory and emits
+// shared-memory loads and stores for accesses through it, not generic ones.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t* __restrict__ sfa, const uint32_t* __restrict__ sfb,
                     const __grid_constant__ OutSet out, int M, int N, int K, int splits, int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* sf_full = empty + STAGES;

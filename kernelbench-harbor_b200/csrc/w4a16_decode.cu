@@ -18,10 +18,9 @@
 //
 // Design (HBM-bound: 31.8 MB per call at M=16, K=14336, N=4096):
 //  * The N axis is cut into 256-column strips (32 packed words = 128 B per K
-//    row); the K axis of each strip into `splits` contiguous ranges, and the
-//    K ranges of a strip form one thread-block cluster (up to 16 CTAs, one per
-//    SM, sized so that every cluster of the grid is resident at once).  M is
-//    cut into 16-row chunks (grid y).
+//    row); the K axis of each strip into `splits` contiguous ranges so that
+//    strips x splits ~= one CTA per SM (split-K).  M is cut into 16-row chunks
+//    (grid y).
 //  * One producer thread initialises the barriers and streams 128-row stages
 //    with TMA (128B-swizzled) into an 8-deep ring: the packed weight tile
 //    (16 KB), the x tile and the scale/zero rows of the stage.
@@ -38,20 +37,22 @@
 //    legacy tensor pipe only does the useful products.
 //  * The fold's per-column factors (s', s' (1024 + z')) are computed once per
 //    warp, one column per lane, and shared through a small per-warp buffer.
-//  * Split-K: each CTA leaves its fp32 partial [16, 256] in shared memory; after
-//    a cluster barrier CTA r sums 16-byte chunks [r * 512 / S, (r+1) * 512 / S)
-//    of the strip over the S partials over DSMEM, in rank order
-//    (deterministic), and stores them.  No workspace beyond the status word.
+//  * Split-K: with splits > 1 the grid has at most one CTA per SM and each CTA
+//    needs a whole SM's shared memory, so all CTAs are resident together.
+//    Each CTA stores its fp32 partial [16, 256] into its workspace slot,
+//    announces it on its strip's arrival counter (release) and waits (bounded,
+//    acquire) until all S partials of the strip are there; then CTA r sums the
+//    16-byte chunks [r * 512 / S, (r+1) * 512 / S) of the strip over the S
+//    slots in slot order (deterministic), stores them, and zeroes what it read.
+//    The last CTA of the strip to finish resets the counters, so the workspace
+//    is left zeroed.
 //  * Programmatic dependent launch (optional, b200q_set_weight_prefetch): the
 //    kernel lets the next kernel in the stream launch at once and streams the
 //    first ring of weight/scale/zero stages before `griddepcontrol.wait`;
-//    x is read, and y written, only after the wait.  Legal only when the kernel
+//    x is read, and y / the workspace written, only after the wait.  Legal only when the kernel
 //    just before this one in the stream does not write this call's qweight /
 //    scales / zeros (true for inference weights).
-#include <array>
-#include <mutex>
 #include <type_traits>
-#include <vector>
 
 #include "common.cuh"
 
@@ -66,9 +67,8 @@ constexpr int XWARP = NCONS;                 // the x-sum warp
 constexpr int PWARP = NCONS + 1;             // the producer warp
 constexpr int THREADS = (NCONS + 2) * 32;
 constexpr int STAGES = 8;
-constexpr int MAX_CLUSTER = 16;
-constexpr int HEADER_BYTES = 256;  // workspace: [status int | pad]
-constexpr int PRS = STRIP_COLS + 8;  // row pitch (floats) of the CTA partial
+constexpr int MAX_SPLITS = 32;
+constexpr int HEADER_BYTES = 256;  // workspace: [status int | pad] then counters then partials
 
 struct Layout {
   static constexpr int QW = KS * STRIP_WORDS * 4;  // 16 KB
@@ -82,7 +82,7 @@ struct Layout {
   static constexpr int FOLD = NCONS * 32 * 8;  // per-warp fold factors (float2 per lane)
   static constexpr int SMEM = RING + XS + BARS + FOLD + 1024 /*align*/;
   static_assert(STAGE % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
-  static_assert(16 * PRS * 4 <= RING, "the partial must fit in the ring");
+  static_assert(16 * (STRIP_COLS + 8) * 4 <= RING, "the partial must fit in the ring");
 };
 
 // Not volatile: a pure register operation, so the compiler may schedule the
@@ -114,17 +114,20 @@ __device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(saddr));
   return v;
 }
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
+__device__ __forceinline__ int ld_acquire_gpu(const int* a) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
   return v;
 }
-__device__ __forceinline__ int ld_cluster_s32(uint32_t addr) {
-  int v;
-  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
+__device__ __forceinline__ int atom_add_release_gpu(int* a, int v) {
+  int old;
+  asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* a, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -136,21 +139,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     w4a16_decode_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                         const __grid_constant__ OutSet out, int M, int N, int group, int splits,
-                        int n_stages_total, int prefetch, int* __restrict__ status) {
+                        int n_stages_total, int prefetch, uint8_t* __restrict__ ws) {
   using L = Layout;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr int GPS = 8 / FS;  // groups (scale rows) per stage
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   float* xs = reinterpret_cast<float*>(smem + L::RING);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::RING + L::XS);
   uint64_t* empty = full + STAGES;
   uint64_t* xready = empty + STAGES;
   __shared__ int s_err;
-  __shared__ int s_any_err;
+  int* status = reinterpret_cast<int*>(ws);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int strip = blockIdx.x / splits, split = blockIdx.x % splits;  // split == cluster rank
+  const int strip = blockIdx.x / splits, split = blockIdx.x % splits;
   const int mchunk = blockIdx.y;
   const int st0 = (int)((long long)split * n_stages_total / splits);
   const int st1 = (int)((long long)(split + 1) * n_stages_total / splits);
@@ -180,6 +183,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int fill = nst < STAGES ? nst : STAGES;
   if (producer) {
     if (prefetch) pdl_trigger();
+    prefetch_tmap(&tm_qw);
+    prefetch_tmap(&tm_s);
+    prefetch_tmap(&tm_z);
+    prefetch_tmap(&tm_x);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCONS / 2 + 1);
@@ -386,41 +393,57 @@ __global__ void __launch_bounds__(THREADS, 1)
   pdl_wait();  // y may still be in use by the previous kernel
 
   // -------------------------------------------------------------------- epilogue
-  // 1. this CTA's partial [16, 256] fp32 (sum of the two stage parities) in
-  //    shared memory at the start of the (now idle) ring: part[row * PRS +
-  //    word * 8 + nibble]; a thread's (row, word) holds 4 consecutive nibbles,
-  //    one float4, and the padded row pitch halves the store conflicts;
-  // 2. cluster barrier; CTA r sums its chunks over the cluster's partials in
-  //    rank order and stores them; 3. cluster barrier (partials stay readable).
+  // this CTA's partial [16, 256] fp32 = sum of the two stage parities, as
+  // float4s of (row, word, 4 nibbles): parity-1 warps leave theirs in shared
+  // memory, parity-0 warps add their own and store the sum (with splits == 1
+  // back into shared memory, otherwise into the CTA's workspace slot, row-major
+  // [16][256])
+  constexpr int PRS = STRIP_COLS + 8;  // padded row pitch of the shared partial (floats)
   float* part = reinterpret_cast<float*>(smem);
+  const int rows_here = min(16, M - mchunk * 16);
+  const int tid = threadIdx.x;
+  const size_t strip_id = (size_t)mchunk * (gridDim.x / splits) + strip;
+  const int n_strips = gridDim.y * (gridDim.x / splits);
+  int* arrive = reinterpret_cast<int*>(ws + HEADER_BYTES);
+  int* depart = arrive + n_strips;
+  float* slots = reinterpret_cast<float*>(ws + HEADER_BYTES + (((size_t)n_strips * 8 + 255) & ~size_t(255)));
+  float* my_slot = slots + (strip_id * splits + split) * (16 * STRIP_COLS);
   if (warp < NCONS) {
-    float4* dst[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      dst[r] = reinterpret_cast<float4*>(part + (g + 8 * (r >> 1)) * PRS + (cg * 8 + 2 * c + (r & 1)) * 8 + 4 * th);
-    if (par == 1) {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) *dst[r] = make_float4(tot[0][r], tot[1][r], tot[2][r], tot[3][r]);
+    for (int r = 0; r < 4; ++r) {
+      const int row = g + 8 * (r >> 1), word = cg * 8 + 2 * c + (r & 1);
+      float4* sp = reinterpret_cast<float4*>(part + row * PRS + word * 8 + 4 * th);
+      if (par == 1) *sp = make_float4(tot[0][r], tot[1][r], tot[2][r], tot[3][r]);
     }
     named_barrier_sync(1, NCONS * 32);
     if (par == 0) {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const float4 o = *dst[r];
-        *dst[r] = make_float4(o.x + tot[0][r], o.y + tot[1][r], o.z + tot[2][r], o.w + tot[3][r]);
+        const int row = g + 8 * (r >> 1), word = cg * 8 + 2 * c + (r & 1);
+        float4* sp = reinterpret_cast<float4*>(part + row * PRS + word * 8 + 4 * th);
+        const float4 o = *sp;
+        const float4 v = make_float4(o.x + tot[0][r], o.y + tot[1][r], o.z + tot[2][r], o.w + tot[3][r]);
+        if (splits == 1)
+          *sp = v;
+        else
+          __stcg(reinterpret_cast<float4*>(my_slot + row * STRIP_COLS + word * 8 + 4 * th), v);
       }
     }
   }
-  if (threadIdx.x == 0) s_any_err = s_err;
-  if (splits > 1) cluster_sync(); else __syncthreads();
-
-  const int rows_here = min(16, M - mchunk * 16);
-  const int tid = threadIdx.x;
-  // any CTA of the cluster that gave up a wait leaves its partial incomplete:
-  // then nobody in the cluster stores
-  if (splits > 1 && tid < splits) {
-    const int e = ld_cluster_s32(map_shared_rank(smem_u32(&s_any_err), (uint32_t)tid));
-    if (e) atomicOr(&s_err, 1);
+  __syncthreads();
+  if (splits > 1 && tid == 0 && !s_err) {
+    // publish this partial; wait for the strip's other partials
+    // the CTA barrier orders every thread's slot stores before this release
+    atom_add_release_gpu(&arrive[strip_id], 1);
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0; ld_acquire_gpu(&arrive[strip_id]) < splits; ++i) {
+      if ((i & 63) == 63 && globaltimer() - t0 > B200Q_WAIT_NS) {
+        atomicOr(status, B200Q_DEV_ERR_TIMEOUT);
+        s_err = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
   }
   if (out.world > 1 && tid == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
   __syncthreads();
@@ -430,26 +453,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int ch = c0 + tid; ch < c1; ch += THREADS) {
       const int row = ch >> 5, cc = ch & 31;
       const int gcol = strip * STRIP_COLS + cc * 8;
-      if (row >= rows_here || gcol >= N) continue;  // N % 32 == 0: a chunk is wholly inside or outside
-      const uint32_t off = smem_u32(part + row * PRS + cc * 8);
       float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-      // peers' partials in batches of 4 (8 DSMEM loads in flight), summed in rank order
-      for (int p0 = 0; p0 < splits; p0 += 4) {
-        float4 a0[4], a1[4];
+      if (splits == 1) {
+        v0 = *reinterpret_cast<const float4*>(part + row * PRS + cc * 8);
+        v1 = *reinterpret_cast<const float4*>(part + row * PRS + cc * 8 + 4);
+      } else {
+        // the strip's slots in batches of 8 (16 loads in flight), summed in
+        // slot order; each chunk has exactly one reader, which zeroes it
+        float4* src = reinterpret_cast<float4*>(slots + strip_id * splits * (16 * STRIP_COLS) + ch * 8);
+        constexpr int SLOT4 = 16 * STRIP_COLS / 4;
+        for (int p0 = 0; p0 < splits; p0 += 8) {
+          float4 a0[8], a1[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (p0 + j < splits) {
-            const uint32_t a = splits > 1 ? map_shared_rank(off, (uint32_t)(p0 + j)) : off;
-            a0[j] = splits > 1 ? ld_cluster_f4(a) : lds_f4(a);
-            a1[j] = splits > 1 ? ld_cluster_f4(a + 16) : lds_f4(a + 16);
-          }
+          for (int j = 0; j < 8; ++j)
+            if (p0 + j < splits) {
+              a0[j] = __ldcg(src + (p0 + j) * SLOT4);
+              a1[j] = __ldcg(src + (p0 + j) * SLOT4 + 1);
+            }
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (p0 + j < splits) {
-            v0.x += a0[j].x, v0.y += a0[j].y, v0.z += a0[j].z, v0.w += a0[j].w;
-            v1.x += a1[j].x, v1.y += a1[j].y, v1.z += a1[j].z, v1.w += a1[j].w;
-          }
+          for (int j = 0; j < 8; ++j)
+            if (p0 + j < splits) {
+              v0.x += a0[j].x, v0.y += a0[j].y, v0.z += a0[j].z, v0.w += a0[j].w;
+              v1.x += a1[j].x, v1.y += a1[j].y, v1.z += a1[j].z, v1.w += a1[j].w;
+              __stcg(src + (p0 + j) * SLOT4, make_float4(0.f, 0.f, 0.f, 0.f));
+              __stcg(src + (p0 + j) * SLOT4 + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+            }
+        }
       }
+      if (row >= rows_here || gcol >= N) continue;  // N % 32 == 0: a chunk is wholly inside or outside
       uint4 o;
       if (!BF16) {
         __half2 h0 = __floats2half2_rn(v0.x, v0.y), h1 = __floats2half2_rn(v0.z, v0.w);
@@ -467,7 +498,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                                   gcol) = o;
     }
   }
-  if (splits > 1) cluster_sync();  // no CTA exits while its partial may still be read
+  if (splits > 1) {
+    // the last CTA of the strip to finish its reads resets the counters
+    __syncthreads();
+    if (tid == 0 && atom_add_acq_rel_gpu(&depart[strip_id], 1) == splits - 1) {
+      arrive[strip_id] = 0;
+      depart[strip_id] = 0;
+    }
+  }
   if (out.world > 1) {
     __syncthreads();
     if (threadIdx.x < 32) peer_finish(out, status);
@@ -476,6 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 struct Plan {
   int mchunks, strips, splits, n_stages;
+  size_t ws_bytes;
 };
 
 Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
@@ -484,60 +523,32 @@ Plan plan(int64_t M, int64_t N, int64_t K, int sms) {
   if (p.mchunks < 1) p.mchunks = 1;
   p.strips = (int)((N + STRIP_COLS - 1) / STRIP_COLS);
   p.n_stages = (int)((K + KS - 1) / KS);
+  // at most one CTA per SM in total when splitting: the CTAs of a strip wait
+  // for one another, so all of them must be resident at once
   int sp = sms / (p.strips * p.mchunks);
   if (sp < 1) sp = 1;
   if (sp > p.n_stages) sp = p.n_stages;
-  if (sp > MAX_CLUSTER) sp = MAX_CLUSTER;
+  if (sp > MAX_SPLITS) sp = MAX_SPLITS;
+  // a CTA's time is its stage pairs (the two parities run side by side): the
+  // fewest splits with the same largest pair count per CTA (112 stages: 8
+  // splits of 14 stages rather than 9 of 12 or 13), which also shrinks the
+  // reduction
+  auto pairs = [&](int k) { return ((p.n_stages + k - 1) / k + 1) / 2; };
+  while (sp > 1 && pairs(sp - 1) == pairs(sp)) --sp;
   p.splits = sp;
+  const size_t n_strips = (size_t)p.strips * p.mchunks;
+  p.ws_bytes = HEADER_BYTES + ((n_strips * 8 + 255) & ~size_t(255)) +
+               (sp > 1 ? n_strips * sp * 16 * STRIP_COLS * sizeof(float) : 0);
   return p;
 }
 
-// Largest cluster size <= want whose clusters (n_clusters of them) are all
-// resident at once; cached per (device, kernel, n_clusters, want).
-template <class Kern>
-static int fit_cluster(Kern kern, int want, int n_clusters) {
-  static std::mutex mu;
-  static std::vector<std::array<long long, 5>> cache;  // device, kernel, n_clusters, want, result
-  const int dev = current_device();
-  const long long kid = (long long)reinterpret_cast<uintptr_t>(reinterpret_cast<const void*>(kern));
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    for (auto& e : cache)
-      if (e[0] == dev && e[1] == kid && e[2] == n_clusters && e[3] == want) return (int)e[4];
-  }
-  int cs = want;
-  for (; cs > 1; --cs) {
-    cudaLaunchConfig_t q = {};
-    q.gridDim = dim3(cs * n_clusters);
-    q.blockDim = dim3(THREADS);
-    q.dynamicSmemBytes = Layout::SMEM;
-    cudaLaunchAttribute qa[1];
-    qa[0].id = cudaLaunchAttributeClusterDimension;
-    qa[0].val.clusterDim.x = (unsigned)cs;
-    qa[0].val.clusterDim.y = 1;
-    qa[0].val.clusterDim.z = 1;
-    q.attrs = qa;
-    q.numAttrs = 1;
-    int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, kern, &q) == cudaSuccess && active >= n_clusters) break;
-    cudaGetLastError();  // a refused size is not an error of this call
-  }
-  std::lock_guard<std::mutex> lk(mu);
-  cache.push_back({dev, kid, n_clusters, want, cs});
-  return cs;
-}
-
 template <bool BF16, int FS>
-static int launch_t(Plan p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s, const CUtensorMap& z,
-                    const OutSet& y, int M, int N, int group, int* status, cudaStream_t stream) {
+static int launch_t(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s,
+                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, uint8_t* ws,
+                    cudaStream_t stream) {
   auto kern = w4a16_decode_kernel<BF16, FS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::SMEM);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(decode)");
-  if (p.splits > 8) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(decode, non-portable cluster)");
-  }
-  if (p.splits > 1) p.splits = fit_cluster(kern, p.splits, p.strips * p.mchunks);
   // weight prefetch across the launch boundary only for single-GPU outputs:
   // the peer-store variant orders itself through its signal pads
   const int prefetch = (weight_prefetch_enabled() && y.world <= 1) ? 1 : 0;
@@ -546,46 +557,37 @@ static int launch_t(Plan p, const CUtensorMap& qw, const CUtensorMap& x, const C
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = Layout::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (p.splits > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = (unsigned)p.splits;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  if (prefetch) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kern, qw, x, s, z, y, M, N, group, p.splits, p.n_stages, prefetch, status);
+  cfg.numAttrs = prefetch ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, qw, x, s, z, y, M, N, group, p.splits, p.n_stages, prefetch, ws);
   if (e != cudaSuccess) return check_cuda(e, "w4a16 decode launch");
   return check_cuda(cudaGetLastError(), "w4a16 decode launch");
 }
 
 template <bool BF16>
 static int launch_g(const Plan& p, const CUtensorMap& qw, const CUtensorMap& x, const CUtensorMap& s,
-                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, int* status, cudaStream_t stream) {
-  if (group == 32) return launch_t<BF16, 2>(p, qw, x, s, z, y, M, N, group, status, stream);
-  if (group == 64) return launch_t<BF16, 4>(p, qw, x, s, z, y, M, N, group, status, stream);
-  return launch_t<BF16, 8>(p, qw, x, s, z, y, M, N, group, status, stream);
+                    const CUtensorMap& z, const OutSet& y, int M, int N, int group, uint8_t* ws, cudaStream_t stream) {
+  if (group == 32) return launch_t<BF16, 2>(p, qw, x, s, z, y, M, N, group, ws, stream);
+  if (group == 64) return launch_t<BF16, 4>(p, qw, x, s, z, y, M, N, group, ws, stream);
+  return launch_t<BF16, 8>(p, qw, x, s, z, y, M, N, group, ws, stream);
 }
 
 }  // namespace decode
 
-size_t w4a16_decode_ws_bytes(int64_t, int64_t, int64_t, int) { return decode::HEADER_BYTES; }
+size_t w4a16_decode_ws_bytes(int64_t M, int64_t N, int64_t K, int device) {
+  return decode::plan(M, N, K, num_sms(device)).ws_bytes;
+}
 
 int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, const void* zeros, const OutSet& y,
                  int64_t M, int64_t N, int64_t K, int64_t group, int dtype, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream) {
   using namespace decode;
   const Plan p = plan(M, N, K, num_sms(-1));
-  if (!workspace || workspace_bytes < (size_t)HEADER_BYTES)
-    return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(HEADER_BYTES) + " bytes required");
+  if (!workspace || workspace_bytes < p.ws_bytes)
+    return fail(B200Q_ERR_WORKSPACE, "w4a16: workspace of " + std::to_string(p.ws_bytes) + " bytes required");
   if (group != 32 && group != 64 && group != 128 && group != 256)
     return fail(B200Q_ERR_UNSUPPORTED, "w4a16 decode: group must be 32, 64, 128 or 256");
   const CUtensorMapDataType h16 = CU_TENSOR_MAP_DATA_TYPE_UINT16;
@@ -602,10 +604,9 @@ int w4a16_decode(const void* x, const int32_t* qweight, const void* scales, cons
   if ((rc = encode_2d(&tz, h16, zeros, N, K / group, (uint64_t)N * 2, STRIP_COLS, srows,
                       CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  int* status = reinterpret_cast<int*>(workspace);
-  if (dtype == B200Q_DTYPE_BF16)
-    return launch_g<true>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, status, stream);
-  return launch_g<false>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, status, stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  if (dtype == B200Q_DTYPE_BF16) return launch_g<true>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, ws, stream);
+  return launch_g<false>(p, tqw, tx, ts, tz, y, (int)M, (int)N, (int)group, ws, stream);
 }
 
 }  // namespace b200q

@@ -90,9 +90,9 @@ extern "C" int b200q_w4a16_gemm_noalloc(const void* x, const int32_t* qweight, c
   if ((rc = scratch_address(device, &scratch))) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // cleared before each call: the 256-byte status header and the split-K
-  // tickets (at most 2 row chunks x one per 256-column strip); the kernel
+  // counters (two per 256-column strip and 16-row chunk, at most 2 chunks); the kernel
   // overwrites its partial slots before reading them and zeroes them after
-  const size_t tickets = ((size_t)2 * ((N + 255) / 256) * 4 + 255) & ~size_t(255);
+  const size_t tickets = ((size_t)2 * ((N + 255) / 256) * 8 + 255) & ~size_t(255);
   const size_t clear = need < 256 + tickets ? need : 256 + tickets;
   if ((rc = check_cuda(cudaMemsetAsync(scratch, 0, clear, st), "noalloc scratch clear"))) return rc;
   return w4a16_decode(x, qweight, scales, zeros, single_out(y, N), M, N, K, group, dtype, scratch, NOALLOC_SCRATCH_BYTES, st);

@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t X_BYTES = C::X_BYTES, OFF_X = C::OFF_X, OFF_B = C::OFF_B, OFF_WQ = C::OFF_WQ,
                      OFF_S = C::OFF_S, OFF_Z = C::OFF_Z, OFF_BAR = C::OFF_BAR;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* x_full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* x_empty = x_full + SX;
   uint64_t* w_full = x_empty + SX;
