@@ -331,9 +331,12 @@ def run_siblings(device, steps, warmup, sampler):
         sets = [[t.to(device) for t in smoothquant_inputs(M, K, N, seed=100 + i)[:4]] for i in range(4)]
         us = time_calls(lambda i: ops.w8a8_gemm(*sets[i]), 4, steps, warmup, 1, sampler, True) * 1e3
         b = M * K + K * N + 2 * M + 2 * N + 2 * M * N
+        tops = 2 * M * N * K / us / 1e6
         out[f"w8a8_m{M}"] = {"us_per_call": round(us, 3), "GB_s": round(b / us / 1e3, 1),
-                             "TOPS": round(2 * M * N * K / us / 1e6, 1),
-                             "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4)}
+                             "TOPS": round(tops, 1),
+                             "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4),
+                             "tensor_frac": round(tops / (2 * peaks["tflops"]), 4),
+                             "tensor_peak": "2 x measured bf16 burst (dense int8 rate is twice bf16)"}
         del sets
     for M in (128, 4096):
         nset = 2 if M > 1024 else 4
@@ -345,9 +348,12 @@ def run_siblings(device, steps, warmup, sampler):
             sets.append([a[0].to(device), a[1].to(device), bq[0].to(device), bq[1].to(device)])
         us = time_calls(lambda i: ops.mxfp8_gemm(*sets[i]), nset, steps, warmup, 1, sampler, True) * 1e3
         b = M * K + N * K + (M + N) * (K // 32) + 2 * M * N
+        tf = 2 * M * N * K / us / 1e6
         out[f"mxfp8_m{M}"] = {"us_per_call": round(us, 3), "GB_s": round(b / us / 1e3, 1),
-                              "TFLOP_s": round(2 * M * N * K / us / 1e6, 1),
-                              "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4)}
+                              "TFLOP_s": round(tf, 1),
+                              "hbm_frac": round(b / us / 1e3 / peaks["hbm_gbs"], 4),
+                              "tensor_frac": round(tf / (2 * peaks["tflops"]), 4),
+                              "tensor_peak": "2 x measured bf16 burst (dense fp8 rate is twice bf16)"}
         del sets
     # MoE: Mixtral shape, one input set (its 8 experts x 3 W4A16 weights = 749 MB > L2)
     T, D, H, E = 512, 4096, 14336, 8
@@ -415,6 +421,35 @@ def run_next_rows(device, steps, warmup, sampler):
     out["multi_lora_llama3_8b_r16_t64"] = {"us_per_call": round(us, 1),
                                            "note": "int8 base weight packed on the GPU inside every call"}
     return out
+
+
+def run_mxfp8_sharded(world, rank, device, steps, warmup, sampler):
+    """MXFP8 M=4096 (K=14336, N=4096) with B column-sharded over the ranks and
+    the all-gather fused into the GEMM epilogue (PeerGatherMXFP8); CUDA graph,
+    CUDA events, max over ranks.  Parity: one call against the per-shard plain
+    GEMMs gathered over NCCL, bit for bit."""
+    from kernelbench_harbor_b200 import ops, parallel
+    from kernelbench_harbor_b200.mx import quantize_mxfp8
+    M, K, N = 4096, K_DIM, N_DIM
+    n = N // world
+    g = torch.Generator(device=device).manual_seed(200)
+    sets = []
+    for i in range(2):
+        a = quantize_mxfp8(torch.randn(M, K, generator=g, device=device).half())
+        b = quantize_mxfp8((torch.randn(N, K, generator=g, device=device) * 0.02).half())
+        sets.append((a[0], a[1], b[0][rank * n:(rank + 1) * n].contiguous(),
+                     b[1][rank * n:(rank + 1) * n].contiguous()))
+    mod = parallel.PeerGatherMXFP8()
+    us = time_calls(lambda i: mod(*sets[i]), 2, steps, warmup, world, sampler, True) * 1e3
+    y = mod(*sets[0]).clone()
+    ref = parallel.gather_columns(ops.mxfp8_gemm(*sets[0]), world)
+    ok = torch.tensor([1 if torch.equal(y, ref) else 0], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    tf = 2 * M * N * K / us / 1e6
+    return {"mxfp8_m4096_sharded": {"us_per_call": round(us, 2), "TFLOP_s": round(tf, 1),
+                                    "tensor_frac": round(tf / (2 * load_peaks()["tflops"] * world), 4),
+                                    "parity_vs_per_shard": bool(ok.item()),
+                                    "parallelism": f"B N-sharded x{world}, gather fused in the epilogue"}}
 
 
 def run_siblings_multi(world, rank, device, steps, warmup, sampler):
@@ -599,6 +634,8 @@ def main():
         siblings = run_siblings(device, args.steps, args.warmup, ClockSampler(device.index))
     elif world > 1 and not args.no_siblings:
         siblings = run_siblings_multi(world, rank, device, args.steps, args.warmup, ClockSampler(device.index))
+        siblings.update(run_mxfp8_sharded(world, rank, device, args.steps, args.warmup,
+                                          ClockSampler(device.index)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -640,7 +677,9 @@ def main():
                 "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
                 **({"parity": {"w4a16_gather": {str(k): v for k, v in parity.items()},
                                "ep_moe": (siblings or {}).get("moe_ep_top2_t512", {}).get(
-                                   "parity_vs_single_gpu")}} if world > 1 else {}),
+                                   "parity_vs_single_gpu"),
+                               "mxfp8_gather": (siblings or {}).get("mxfp8_m4096_sharded", {}).get(
+                                   "parity_vs_per_shard")}} if world > 1 else {}),
                 # our kernels per step: the GEMM (with the gather fused into it for --gather peer)
                 "gpu_launches": args.steps}
         print(json.dumps(line), flush=True)

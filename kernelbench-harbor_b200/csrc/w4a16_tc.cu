@@ -29,6 +29,8 @@
 // which yields columns (0,4), (1,5), (2,6), (3,7) of a word; the B operand is
 // stored in that column order and the epilogue undoes the permutation in
 // registers.
+#include <algorithm>
+
 #include "w4a16_dq.cuh"
 
 namespace b200q {
@@ -72,7 +74,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* b_empty = b_full + S2;
   uint64_t* acc_full = b_empty + S2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  __shared__ int s_err;
+  __shared__ int s_err, s_clu_err;
 
   int* status = reinterpret_cast<int*>(ws);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -394,7 +396,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (mb == 0 && threadIdx.x == 0 && !s_err && !peer_wait_arrivals(out, status)) s_err = 1;
     cluster_sync();
-    if (!s_err) {
+    // a CTA of the cluster that gave up a wait sent incomplete rows: then no
+    // owner of the cluster writes this pass (every CTA's s_err is final here)
+    if (threadIdx.x == 0) s_clu_err = 0;
+    __syncthreads();
+    if (threadIdx.x < S) {
+      int e;
+      asm volatile("ld.shared::cluster.s32 %0, [%1];"
+                   : "=r"(e)
+                   : "r"(map_shared_rank(smem_u32(&s_err), threadIdx.x)));
+      if (e) atomicOr(&s_clu_err, 1);
+    }
+    __syncthreads();
+    if (!s_clu_err) {
       const float* buf = reinterpret_cast<const float*>(smem);
       const int r0 = (int)(rank * BM / S), nr = (int)((rank + 1) * BM / S) - r0;
       for (int e = threadIdx.x * 4; e < nr * BN; e += THREADS * 4) {
@@ -408,7 +422,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           acc4.w += p4.w;
         }
         const int row = m0 + mb * BM + r0 + lr, col = n0 + c;
-        if (row < M && col < N) {
+        if (row < m_end && col < N) {
           uint2 packed;
           if (!BF16) {
             packed.x = as_u32(__floats2half2_rn(acc4.x, acc4.y));
@@ -592,8 +606,51 @@ int w4a16_tc_grouped(const void* x, const int32_t* qw, const void* sc, const voi
   const int tiles_m = (int)((rows + 2 * BM - 1) / (2 * BM) + E);
   const int tiles_n = (int)((N + (glu ? BN / 2 : BN) - 1) / (glu ? BN / 2 : BN));
   OutSet out = single_out(y, N);
-  kern<<<dim3(tiles_n, tiles_m, 1), THREADS, smem, stream>>>(tx, twq, ts, tz, out, (int)rows, (int)N, (int)K,
-                                                             (int)group, 1, reinterpret_cast<uint8_t*>(workspace), g);
+  // split-K (plain grouped mode): when the experts' tiles cannot fill the
+  // SMs (expert-parallel ranks hold few rows per expert), the K ranges of a
+  // tile form a cluster, as in the dense kernel.  The tile count is only known
+  // on the device; the estimate is one 256-row tile per expert or per 256
+  // rows, whichever is more (tiles launched beyond the real ones exit at once).
+  int splits = 1;
+  if (!glu) {
+    const int nk = (int)((K + BK - 1) / BK);
+    const int est_m = (int)std::min<int64_t>(tiles_m, std::max<int64_t>(E, (rows + 2 * BM - 1) / (2 * BM)));
+    const int sms = num_sms(-1);
+    splits = sms / std::max(1, est_m * tiles_n);
+    splits = std::max(1, std::min(splits, std::min(MAX_SPLITS, nk / 4)));
+    while (splits > 1) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(tiles_n, est_m, splits);
+      q.blockDim = dim3(THREADS);
+      q.dynamicSmemBytes = smem;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 1;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = (unsigned)splits;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int active = 0;
+      if (cudaOccupancyMaxActiveClusters(&active, kern, &q) == cudaSuccess && active >= est_m * tiles_n) break;
+      cudaGetLastError();
+      --splits;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles_n, tiles_m, splits);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tx, twq, ts, tz, out, (int)rows, (int)N, (int)K, (int)group, splits,
+                         reinterpret_cast<uint8_t*>(workspace), g);
+  if (e != cudaSuccess) return check_cuda(e, "w4a16 grouped launch");
   return check_cuda(cudaGetLastError(), "w4a16 grouped launch");
 }
 

@@ -2,12 +2,14 @@
 kernel) and its fused SiLU * mul epilogue.
 
 * the fused gate/up launch equals the unfused grouped gate and up GEMMs
-  followed by silu_mul, bit for bit (same rounding points by construction);
+  followed by silu_mul (same rounding points; the unfused launches may
+  split K, so up to one rounding of g and u apart);
 * every expert's rows of the grouped GEMM match that expert's plain W4A16
   GEMM against the fp32 ground truth (oracle restatement of the dequant);
 * ragged and skewed groupings: empty experts, one expert taking every row,
   row counts that are not multiples of the 128-row tile, bf16, group 32 / 64
   (two scale rows per 64-deep stage);
+* split-K grouped launches (few expert tiles, long K) are deterministic;
 * the grouped MoE module equals the per-expert (unfused) module within the
   rounding of the split-K reductions the per-expert path may choose.
 """
@@ -42,6 +44,9 @@ CASES = [
     ([0, 0, 0, 300], 256, 512, 64, "fp16"),
     ([17, 33, 1, 128], 1024, 256, 32, "bf16"),
     ([128] * 8, 4096, 1024, 128, "fp16"),
+    # one expert with ~128 rows and a long K (an expert-parallel rank's down
+    # projection): the grouped launch splits K over a cluster
+    ([120], 14336, 4096, 128, "fp16"),
 ]
 
 
@@ -84,7 +89,12 @@ def test_fused_glu_bit_exact_vs_unfused(counts, K, N, group, dtype):
     hu = ops.moe_grouped_gemm(x, off, uq, us, uz, group)
     ref = ops.silu_mul(hg, hu)
     torch.cuda.synchronize()
-    assert torch.equal(h, ref)
+    # the unfused grouped GEMMs may split K over a cluster (few expert tiles)
+    # where the fused gate/up launch does not: the fp32 sums then differ in
+    # order, so g and u can differ by one rounding; otherwise the two are the
+    # same arithmetic
+    top = ref.float().abs().max().item()
+    torch.testing.assert_close(h.float(), ref.float(), rtol=5e-3, atol=5e-3 * max(top, 1.0))
     assert ops.device_status() == 0
 
 
@@ -120,3 +130,14 @@ def test_grouped_moe_cuda_graph():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(y0, y1)
+
+
+def test_grouped_split_k_deterministic():
+    from kernelbench_harbor_b200 import ops
+    x, _, _, _ = w4a16_inputs(120, 14336, 32, 128, "fp16", seed=9)
+    q, s, z = _stacked(1, 14336, 4096, 128, "fp16", seed=300)
+    off = _offsets([120])
+    ys = [ops.moe_grouped_gemm(x.cuda(), off, q, s, z, 128) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    assert ops.device_status() == 0
