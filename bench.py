@@ -657,6 +657,10 @@ def main():
             pk = peaks["tflops"] * world
             roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s"}
         roof["frac"] = round(ach / pk, 4)
+        if head["bound"] == "tensor":
+            # the timed region is a loop of `steps` calls: long regions run
+            # under the 1 kW power cap, so the sustained GEMM peak applies too
+            roof["frac_of_sustained"] = round(ach / (peaks["tflops_sustained"] * world), 4)
         roof["peak_source"] = ("measured (MEASURED_PEAKS.json, burst)" if peaks["source"] == "measured"
                                else "fallback") + (f" x {world} GPUs" if world > 1 else "")
         # DRAM bytes (read + write) of one launch of the headline kernel, from
