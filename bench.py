@@ -489,12 +489,21 @@ def run_siblings_multi(world, rank, device, steps, warmup, sampler):
             q.append(qe), s_.append(se), z.append(ze)
         full += [torch.stack(q), torch.stack(s_), torch.stack(z)]
     ref = QuantizedMoE()(x_all, logits_all, *full)[rank * tl:(rank + 1) * tl]
-    ok = torch.tensor([1 if torch.equal(y, ref) else 0], device=device)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    # a rank holding few expert tiles splits K in the down projection where
+    # the single-GPU module does not, so the fp32 sums may differ in order:
+    # the check is the benchmark's tolerance, with the bit-identity reported
+    diff = (y.float() - ref.float()).abs().max()
+    close = torch.allclose(y.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    flags = torch.tensor([1 if close else 0, 1 if torch.equal(y, ref) else 0], device=device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    dist.all_reduce(diff, op=dist.ReduceOp.MAX)
+    ok = flags[0]
     del full
     torch.cuda.empty_cache()
     return {"moe_ep_top2_t512": {"us_per_call": round(us, 1), "TFLOP_s": round(fl / us / 1e6, 1),
                                  "parity_vs_single_gpu": bool(ok.item()),
+                                 "parity_check": "allclose(rtol=atol=1e-2) against the single-GPU module",
+                                 "bit_identical": bool(flags[1].item()), "max_abs_diff": round(float(diff), 6),
                                  "experts_per_gpu": epr, "tokens_per_gpu": tl, "steps": msteps,
                                  "timing": "CUDA graph (fixed-capacity all-to-alls, no host "
                                            "synchronisation), CUDA events, max over ranks"}}
