@@ -234,6 +234,11 @@ def run_ours(args, world, rank, device, peaks):
         us = ms * 1e3
         if world > 1:
             parity[M] = sharded_parity(model, sets[0], world)
+            # the same shards through the plain single-GPU entry point (no
+            # peer stores, no cross-rank ordering): the compute part of the
+            # fused-gather time
+            ms_local = time_calls(lambda i: ops.w4a16_gemm(*sets[i], GROUP), n_sets, args.steps, args.warmup,
+                                  world, sampler, use_graph)
         ab = algorithmic_bytes(M, N_DIM, K_DIM, GROUP)
         fl = flops(M, N_DIM, K_DIM)
         t_hbm = ab / (peaks["hbm_gbs"] * 1e9 * world)
@@ -243,6 +248,8 @@ def run_ours(args, world, rank, device, peaks):
                     "TFLOP_s": round(fl / (us * 1e-6) / 1e12, 1), "bound": bound,
                     "roofline_frac": round((t_hbm if bound == "hbm" else t_ten) / (us * 1e-6), 4),
                     "l2": f"{n_sets} rotating input sets of {set_bytes / 2**20:.0f} MiB"}
+        if world > 1:
+            sweep[M]["shard_gemm_only_us"] = round(ms_local * 1e3, 3)
         if world == 1 and M <= 16:
             # the same calls with weight prefetch across the launch boundary
             # (programmatic dependent launch; weights are never written here)
