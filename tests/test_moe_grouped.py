@@ -47,6 +47,9 @@ CASES = [
     # one expert with ~128 rows and a long K (an expert-parallel rank's down
     # projection): the grouped launch splits K over a cluster
     ([120], 14336, 4096, 128, "fp16"),
+    # an expert-parallel rank of 2: four experts of ~256 rows (two 128-row
+    # blocks per tile), long K, a 2-way split
+    ([250, 262, 238, 274], 14336, 4096, 128, "fp16"),
 ]
 
 
