@@ -278,14 +278,17 @@ class ExpertParallelMoE(nn.Module):
         counts = torch.zeros(P, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
         starts = torch.cumsum(counts, 0) - counts
         slot = dest * C + torch.arange(2 * T, device=dev) - starts[dest]
-        send = x.new_empty((P * C, D))
-        send[slot] = x[pair_t[order]]
-        send_eid = torch.full((P * C,), -1, dtype=torch.int64, device=dev)
-        send_eid[slot] = pair_e[order] - dest * epr
-        recv = torch.empty_like(send)
-        recv_eid = torch.empty_like(send_eid)
-        dist.all_to_all_single(recv, send, group=self.pg)
-        dist.all_to_all_single(recv_eid, send_eid, group=self.pg)
+        # each row carries its local expert id (-1: empty slot) in an extra
+        # column (small integers are exact in fp16 / bf16), so one all-to-all
+        # moves rows and ids; 8 extra columns keep rows 16-byte pitched
+        send = x.new_empty((P * C, D + 8))
+        send[:, D] = -1
+        send[slot, :D] = x[pair_t[order]]
+        send[slot, D] = (pair_e[order] - dest * epr).to(x.dtype)
+        recv2 = torch.empty_like(send)
+        dist.all_to_all_single(recv2, send, group=self.pg)
+        recv = recv2[:, :D]
+        recv_eid = recv2[:, D].to(torch.int64)
         # this rank's experts over the received rows, regrouped by expert (empty slots last)
         key = torch.where(recv_eid >= 0, recv_eid, torch.full_like(recv_eid, epr))
         o2 = torch.argsort(key * (P * C) + torch.arange(P * C, device=dev))
@@ -302,9 +305,9 @@ class ExpertParallelMoE(nn.Module):
                 if offs[el + 1] > offs[el]:
                     y_sorted[offs[el]:offs[el + 1]] = self.expert(el, rows[offs[el]:offs[el + 1]].contiguous(),
                                                                   local_weights)
-        y_recv = torch.empty_like(recv)
+        y_recv = torch.empty((P * C, D), dtype=x.dtype, device=dev)
         y_recv[o2] = y_sorted
-        back = torch.empty_like(send)
+        back = torch.empty_like(y_recv)
         dist.all_to_all_single(back, y_recv, group=self.pg)
         ye = torch.empty((2 * T, D), dtype=x.dtype, device=dev)
         ye[order] = back[slot]
