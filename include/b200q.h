@@ -116,6 +116,32 @@ int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dty
 int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
                       int dtype, void* stream);
 
+/* Expert-parallel exchange helpers for a rank of P holding E/P experts, with C
+ * row slots per (source, destination) rank pair (the benchmark's
+ * expert-parallel MoE; the reference MoE is single-GPU, generate_tasks.py:
+ * 368-378, so these have no counterpart there).  Rows are fp16/bf16 with
+ * D % 8 == 0; exchanged rows carry D + 8 values, value D being the local
+ * expert index of the row as a small integer (-1: empty slot).
+ * ep_pack: from b200q_moe_route's offsets / slot_token / token_slot over this
+ * rank's T tokens, send [P * C, D + 8] gets in slot d * C + j the j-th row
+ * routed to rank d, and pair_slot [T, 2] each token's two slots (to pass as
+ * b200q_moe_combine's token_slot on the returned rows).  C >= 2 T. */
+int b200q_ep_pack(const void* x, int64_t T, int64_t D, int dtype, const int32_t* offsets, const int32_t* slot_token,
+                  const int32_t* token_slot, int64_t E, int64_t P, int64_t C, void* send, int32_t* pair_slot,
+                  void* stream);
+
+/* ep_regroup: the R received rows [R, D + 8] ordered stably by local expert:
+ * loc_offsets [n_local + 1], src [R] (received row at grouped position j, -1
+ * past the last), row_pos [R] (grouped position of received row r, -1 for an
+ * empty slot).  One CTA; no host synchronisation. */
+int b200q_ep_regroup(const void* recv, int64_t R, int64_t D, int dtype, int64_t n_local, int32_t* loc_offsets,
+                     int32_t* src, int32_t* row_pos, void* stream);
+
+/* ep_gather: dst[j, :D] = src[idx[j], :D] for j < n with idx[j] >= 0 (other
+ * rows untouched); row pitches in elements, multiples of 8. */
+int b200q_ep_gather(const void* src, int64_t src_pitch, const int32_t* idx, int64_t n, int64_t D, void* dst,
+                    int64_t dst_pitch, void* stream);
+
 /* Bytes of zero-initialised workspace b200q_mxfp8_gemm needs (the status
  * word: split-K is reduced over DSMEM inside a thread-block cluster). */
 size_t b200q_mxfp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int device);

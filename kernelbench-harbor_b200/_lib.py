@@ -43,6 +43,10 @@ SIGNATURES = {
     "b200q_moe_route": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                        _c_vp]),
     "b200q_moe_gather": (ctypes.c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),
+    "b200q_ep_pack": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64,
+                                     _c_i64, _c_vp, _c_vp, _c_vp]),
+    "b200q_ep_regroup": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, ctypes.c_int, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "b200q_ep_gather": (ctypes.c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_vp]),
     "b200q_silu_mul": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_i64, ctypes.c_int, _c_vp]),
     "b200q_moe_combine": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_int, _c_vp]),
     "b200q_w4a16_gemm_noalloc": (ctypes.c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64,

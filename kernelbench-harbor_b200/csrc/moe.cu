@@ -228,3 +228,177 @@ int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gat
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Expert-parallel exchange helpers (the benchmark's expert-parallel MoE; the
+// reference MoE is single-GPU, generate_tasks.py:368-378).  With P ranks,
+// E / P experts per rank and C row slots per (source, destination) pair:
+//   ep_pack     fills this rank's send buffer [P * C, D + 8] from its routed
+//               tokens: slot d * C + j holds the j-th row routed to rank d
+//               (expert-grouped order of moe_route), column D the destination
+//               expert's local index as a small integer in the activation type
+//               (-1: empty slot); pair_slot[t, k] = the slot of token t's k-th row;
+//   ep_regroup  (one CTA) orders the received rows [P * C, D + 8] stably by
+//               local expert: loc_offsets [E/P + 1], src[j] = received row at
+//               grouped position j (-1 past the last), row_pos[r] = grouped
+//               position of received row r (-1: empty slot);
+//   ep_gather   dst[j, :D] = src[idx[j], :D] for idx[j] >= 0, any row pitches.
+namespace b200q {
+namespace moe {
+
+template <class T>
+__global__ void ep_pack_kernel(const uint4* __restrict__ x, int row16, const int32_t* __restrict__ offsets,
+                               const int32_t* __restrict__ slot_token, const int32_t* __restrict__ token_slot, int P,
+                               int C, int epr, T* __restrict__ send, int send_pitch, int32_t* __restrict__ pair_slot) {
+  const int r = blockIdx.x;
+  const int d = r / C, li = r % C;
+  const int base = offsets[d * epr], cnt = offsets[(d + 1) * epr] - base;
+  T* row = send + (size_t)r * send_pitch;
+  const int D = row16 * 8;
+  if (li >= cnt) {
+    if (threadIdx.x < 8) row[D + threadIdx.x] = from_f<T>(threadIdx.x == 0 ? -1.f : 0.f);
+    return;
+  }
+  const int i = base + li;
+  const int t = slot_token[i];
+  int e = d * epr;
+  while (e + 1 < (d + 1) * epr && offsets[e + 1] <= i) ++e;
+  const uint4* src = x + (size_t)t * row16;
+  uint4* dst = reinterpret_cast<uint4*>(row);
+  for (int q = threadIdx.x; q < row16; q += blockDim.x) dst[q] = src[q];
+  if (threadIdx.x < 8) row[D + threadIdx.x] = from_f<T>(threadIdx.x == 0 ? (float)(e - d * epr) : 0.f);
+  if (threadIdx.x == 0) pair_slot[2 * t + (token_slot[2 * t] == i ? 0 : 1)] = r;
+}
+
+template <class T>
+__global__ void __launch_bounds__(1024, 1)
+    ep_regroup_kernel(const T* __restrict__ recv, int pitch, int D, int R, int epr, int32_t* __restrict__ loc_offsets,
+                      int32_t* __restrict__ src, int32_t* __restrict__ row_pos) {
+  __shared__ int s_cnt[MAX_EXPERTS], s_base[MAX_EXPERTS], s_warp[32][65];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < epr; e += blockDim.x) s_cnt[e] = 0;
+  for (int j = tid; j < R; j += blockDim.x) src[j] = -1;
+  __syncthreads();
+  auto eid_of = [&](int r) { return (int)rintf(to_f<T>(recv[(size_t)r * pitch + D])); };
+  for (int r = tid; r < R; r += blockDim.x) {
+    const int e = eid_of(r);
+    if (e >= 0 && e < epr) atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < epr; ++e) {
+      s_base[e] = acc;
+      loc_offsets[e] = acc;
+      acc += s_cnt[e];
+    }
+    loc_offsets[epr] = acc;
+  }
+  __syncthreads();
+  // stable positions, 1024 rows at a time, experts in blocks of 64
+  for (int r0 = 0; r0 < R; r0 += blockDim.x) {
+    const int r = r0 + tid;
+    const int e = r < R ? eid_of(r) : -1;
+    int pos = -1;
+    for (int e0 = 0; e0 < epr; e0 += 64) {
+      const int ne = min(64, epr - e0);
+      for (int k = 0; k < ne; ++k) {
+        const unsigned m = __ballot_sync(0xffffffffu, e == e0 + k);
+        if (lane == 0) s_warp[warp][k] = __popc(m);
+        if (e == e0 + k) pos = __popc(m & ((1u << lane) - 1u));  // rank within the warp
+      }
+      __syncthreads();
+      if (tid < ne) {  // exclusive prefix over the warps, per expert
+        int acc = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+          const int v = s_warp[w][tid];
+          s_warp[w][tid] = acc;
+          acc += v;
+        }
+        s_cnt[e0 + tid] = acc;  // rows of this chunk for the expert
+      }
+      __syncthreads();
+      if (e >= e0 && e < e0 + ne) pos += s_base[e] + s_warp[warp][e - e0];
+      __syncthreads();
+      if (tid < ne) s_base[e0 + tid] += s_cnt[e0 + tid];
+      __syncthreads();
+    }
+    if (r < R) {
+      row_pos[r] = (e >= 0 && e < epr) ? pos : -1;
+      if (e >= 0 && e < epr) src[pos] = r;
+    }
+  }
+}
+
+__global__ void ep_gather_kernel(const uint4* __restrict__ src, int src_pitch16, const int32_t* __restrict__ idx,
+                                 int row16, uint4* __restrict__ dst, int dst_pitch16) {
+  const int j = blockIdx.x;
+  const int s = idx[j];
+  if (s < 0) return;
+  const uint4* a = src + (size_t)s * src_pitch16;
+  uint4* b = dst + (size_t)j * dst_pitch16;
+  for (int q = threadIdx.x; q < row16; q += blockDim.x) b[q] = a[q];
+}
+
+}  // namespace moe
+}  // namespace b200q
+
+extern "C" {
+
+int b200q_ep_pack(const void* x, int64_t T, int64_t D, int dtype, const int32_t* offsets, const int32_t* slot_token,
+                  const int32_t* token_slot, int64_t E, int64_t P, int64_t C, void* send, int32_t* pair_slot,
+                  void* stream) {
+  using namespace b200q;
+  if (T < 0 || D <= 0 || D % 8 || P < 1 || E % P || E > moe::MAX_EXPERTS || C < 0 || P * C > (1ll << 30))
+    return fail(B200Q_ERR_SHAPE, "ep_pack: need D % 8 == 0, E % P == 0, E <= 256");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send)) & 15)
+    return fail(B200Q_ERR_ALIGN, "ep_pack: x and send must be 16-byte aligned");
+  if (P * C == 0) return B200Q_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int epr = (int)(E / P), pitch = (int)D + 8;
+  if (dtype == B200Q_DTYPE_FP16)
+    moe::ep_pack_kernel<__half><<<(unsigned)(P * C), 128, 0, st>>>(
+        reinterpret_cast<const uint4*>(x), (int)(D / 8), offsets, slot_token, token_slot, (int)P, (int)C, epr,
+        reinterpret_cast<__half*>(send), pitch, pair_slot);
+  else if (dtype == B200Q_DTYPE_BF16)
+    moe::ep_pack_kernel<__nv_bfloat16><<<(unsigned)(P * C), 128, 0, st>>>(
+        reinterpret_cast<const uint4*>(x), (int)(D / 8), offsets, slot_token, token_slot, (int)P, (int)C, epr,
+        reinterpret_cast<__nv_bfloat16*>(send), pitch, pair_slot);
+  else
+    return fail(B200Q_ERR_UNSUPPORTED, "ep_pack: dtype must be fp16 or bf16");
+  return check_cuda(cudaGetLastError(), "ep_pack launch");
+}
+
+int b200q_ep_regroup(const void* recv, int64_t R, int64_t D, int dtype, int64_t n_local, int32_t* loc_offsets,
+                     int32_t* src, int32_t* row_pos, void* stream) {
+  using namespace b200q;
+  if (R < 0 || D <= 0 || D % 8 || n_local < 1 || n_local > moe::MAX_EXPERTS || R > (1ll << 30))
+    return fail(B200Q_ERR_SHAPE, "ep_regroup: need D % 8 == 0 and 1 <= n_local <= 256");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == B200Q_DTYPE_FP16)
+    moe::ep_regroup_kernel<__half><<<1, 1024, 0, st>>>(reinterpret_cast<const __half*>(recv), (int)D + 8, (int)D,
+                                                       (int)R, (int)n_local, loc_offsets, src, row_pos);
+  else if (dtype == B200Q_DTYPE_BF16)
+    moe::ep_regroup_kernel<__nv_bfloat16><<<1, 1024, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(recv),
+                                                              (int)D + 8, (int)D, (int)R, (int)n_local, loc_offsets,
+                                                              src, row_pos);
+  else
+    return fail(B200Q_ERR_UNSUPPORTED, "ep_regroup: dtype must be fp16 or bf16");
+  return check_cuda(cudaGetLastError(), "ep_regroup launch");
+}
+
+int b200q_ep_gather(const void* src, int64_t src_pitch, const int32_t* idx, int64_t n, int64_t D, void* dst,
+                    int64_t dst_pitch, void* stream) {
+  using namespace b200q;
+  if (n < 0 || D <= 0 || D % 8 || src_pitch % 8 || dst_pitch % 8 || src_pitch < D || dst_pitch < D)
+    return fail(B200Q_ERR_SHAPE, "ep_gather: D and pitches must be multiples of 8 elements, pitches >= D");
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15)
+    return fail(B200Q_ERR_ALIGN, "ep_gather: pointers must be 16-byte aligned");
+  if (n == 0) return B200Q_OK;
+  moe::ep_gather_kernel<<<(unsigned)n, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(src), (int)(src_pitch / 8), idx, (int)(D / 8), reinterpret_cast<uint4*>(dst),
+      (int)(dst_pitch / 8));
+  return check_cuda(cudaGetLastError(), "ep_gather launch");
+}
+
+}  // extern "C"

@@ -302,6 +302,39 @@ def _(x, offsets, qweight, scales, zeros, group, qweight_up=None, scales_up=None
     return x.new_empty((x.shape[0], qweight.shape[2] * 8))
 
 
+def ep_pack(x: torch.Tensor, offsets: torch.Tensor, slot_token: torch.Tensor, token_slot: torch.Tensor,
+            n_experts: int, world: int, capacity: int):
+    """Send buffer [world * capacity, D + 8] of an expert-parallel exchange
+    (see include/b200q.h) and pair_slot [T, 2] int32."""
+    T, D = x.shape
+    x = _aligned(x)
+    send = torch.empty((world * capacity, D + 8), dtype=x.dtype, device=x.device)
+    pair_slot = torch.empty((T, 2), dtype=torch.int32, device=x.device)
+    _lib.check(_lib.lib().b200q_ep_pack(x.data_ptr(), T, D, _dtype_code(x.dtype), offsets.data_ptr(),
+                                        slot_token.data_ptr(), token_slot.data_ptr(), n_experts, world, capacity,
+                                        send.data_ptr(), pair_slot.data_ptr(), _stream_ptr(x.device)))
+    return send, pair_slot
+
+
+def ep_regroup(recv: torch.Tensor, n_local: int):
+    """(loc_offsets [n_local + 1], src [R], row_pos [R]) int32 for received rows [R, D + 8]."""
+    R, D8 = recv.shape
+    dev = recv.device
+    loc = torch.empty(n_local + 1, dtype=torch.int32, device=dev)
+    src = torch.empty(R, dtype=torch.int32, device=dev)
+    pos = torch.empty(R, dtype=torch.int32, device=dev)
+    _lib.check(_lib.lib().b200q_ep_regroup(recv.data_ptr(), R, D8 - 8, _dtype_code(recv.dtype), n_local,
+                                           loc.data_ptr(), src.data_ptr(), pos.data_ptr(), _stream_ptr(dev)))
+    return loc, src, pos
+
+
+def ep_gather(src: torch.Tensor, idx: torch.Tensor, D: int, out: torch.Tensor) -> torch.Tensor:
+    """out[j, :D] = src[idx[j], :D] where idx[j] >= 0 (2-D row-pitched tensors)."""
+    _lib.check(_lib.lib().b200q_ep_gather(src.data_ptr(), src.stride(0), idx.data_ptr(), idx.numel(), D,
+                                          out.data_ptr(), out.stride(0), _stream_ptr(src.device)))
+    return out
+
+
 def pack_int4(codes: torch.Tensor, offset: int = 0) -> torch.Tensor:
     """4-bit codes [..., N] (int8 / uint8, one per byte) -> int32 [..., N/8]
     packed along N (nibble i of word j = column 8j + i).  offset 0: unsigned

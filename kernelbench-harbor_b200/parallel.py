@@ -243,6 +243,7 @@ class ExpertParallelMoE(nn.Module):
         self.E = n_experts
         self.padded = padded
         self.pg = process_group
+        self._default_ops = route is None and combine is None
         if route is None or combine is None:
             from . import ops
             route = route or (lambda logits: ops.moe_route(logits)[:2])
@@ -259,6 +260,37 @@ class ExpertParallelMoE(nn.Module):
         return self._forward_exact_splits(x, router_logits, local_weights)
 
     def _forward_padded(self, x, router_logits, local_weights):
+        if x.is_cuda and self.expert is None and self._default_ops:
+            return self._forward_padded_cuda(x, router_logits, local_weights)
+        return self._forward_padded_torch(x, router_logits, local_weights)
+
+    def _forward_padded_cuda(self, x, router_logits, local_weights):
+        """The fixed-capacity exchange with the library's kernels for the
+        bookkeeping: moe_route's expert-grouped permutation, ep_pack (send
+        rows with their local expert ids, each token's two slots), one
+        all-to-all, ep_regroup (stable order by local expert), ep_gather into
+        the grouped GEMMs' rows and back, the return all-to-all, and the gated
+        combine reading the returned rows in place."""
+        from . import ops
+        P = dist.get_world_size(self.pg)
+        E, T, D = self.E, x.shape[0], x.shape[1]
+        epr = E // P
+        C = 2 * T
+        _, gates, offsets, slot_token, token_slot = ops.moe_route(router_logits)
+        send, pair_slot = ops.ep_pack(x, offsets, slot_token, token_slot, E, P, C)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.pg)
+        loc, src, pos = ops.ep_regroup(recv, epr)
+        rows = torch.empty((P * C, D), dtype=x.dtype, device=x.device)
+        ops.ep_gather(recv, src, D, rows)
+        y_sorted = _grouped_experts_at(rows, loc, local_weights)
+        y_recv = torch.empty((P * C, D), dtype=x.dtype, device=x.device)
+        ops.ep_gather(y_sorted, pos, D, y_recv)
+        back = torch.empty_like(y_recv)
+        dist.all_to_all_single(back, y_recv, group=self.pg)
+        return self.combine(back, pair_slot, gates)
+
+    def _forward_padded_torch(self, x, router_logits, local_weights):
         """Exchange with fixed-capacity all-to-alls: every (source, destination)
         pair gets C = 2 * T_local row slots (the most one rank can send to
         another), unused slots carry expert id -1.  All counts stay on the
