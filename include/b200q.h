@@ -51,7 +51,9 @@ const char* b200q_last_error(void);
 /* Reads and clears the device status word at the start of a workspace: waits
  * for `stream`, returns 0 when no kernel reported an error, otherwise the
  * or-ed device error bits (1 = a bounded wait timed out). Returns a negative
- * status if the copy itself fails. */
+ * status if the copy itself fails.  After a device error the workspace may
+ * hold a kernel's unfinished split-K counters: zero the whole workspace again
+ * before reusing it. */
 int b200q_workspace_status(void* workspace, void* stream);
 
 /* Weight prefetch across kernel boundaries (off by default; process-wide).
