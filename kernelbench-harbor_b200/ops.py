@@ -443,4 +443,6 @@ def device_status(device: torch.device | None = None) -> int:
     r = _lib.lib().b200q_workspace_status(ws.data_ptr(), _stream_ptr(device))
     if r < 0:
         _lib.check(r)
+    if r > 0:
+        ws.zero_()  # a kernel that gave up may have left split-K counters behind
     return r
