@@ -628,6 +628,24 @@ def profile_case(args) -> int:
             ws += [torch.stack([p[i] for p in parts]) for i in range(3)]
         mod = QuantizedMoE()
         call = lambda: mod(x, logits, *ws)  # noqa: E731
+    elif kind == "ep":
+        # one rank of an expert-parallel MoE (a one-process NCCL group), SIZE
+        # tokens, 4 local experts of the Mixtral shape: the exchange
+        # bookkeeping and the grouped GEMMs as one rank runs them
+        from kernelbench_harbor_b200 import parallel
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29541")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=device)
+        T, D, H, E = size, 4096, 14336, 4
+        g = torch.Generator(device=device).manual_seed(3)
+        x = torch.randn(T, D, generator=g, device=device).half()
+        logits = (x.float() @ (torch.randn(E, D, generator=g, device=device) * 0.02).t()).half()
+        ws = []
+        for j, (kk, nn) in enumerate(((D, H), (D, H), (H, D))):
+            parts = [make_weights(10 * e + j, device, K=kk, N=nn) for e in range(E)]
+            ws += [torch.stack([p[i] for p in parts]) for i in range(3)]
+        mod = parallel.ExpertParallelMoE(E)
+        call = lambda: mod(x, logits, ws)  # noqa: E731
     elif kind == "w8a8":
         from kernelbench_harbor_b200.quant import smoothquant_inputs
         t = [v.to(device) for v in smoothquant_inputs(size, K_DIM, N_DIM, seed=1)[:4]]
@@ -644,6 +662,8 @@ def profile_case(args) -> int:
     for _ in range(args.calls):
         call()
     torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.destroy_process_group()
     print("ok")
     return 0
 
@@ -662,7 +682,8 @@ def main():
     ap.add_argument("--no-siblings", action="store_true")
     ap.add_argument("--profile", default=None,
                     help="KIND=SIZE: run `--calls` untimed calls of one case for a profiler and exit; "
-                         "KIND is w4a16 (SIZE = M), moe (tokens), w8a8 (M), mxfp8 (M)")
+                         "KIND is w4a16 (SIZE = M), moe (tokens), ep (tokens of one "
+                         "expert-parallel rank), w8a8 (M), mxfp8 (M)")
     ap.add_argument("--calls", type=int, default=2)
     ap.add_argument("--prefetch", action="store_true", help="with --profile: weight prefetch on")
     args = ap.parse_args()
