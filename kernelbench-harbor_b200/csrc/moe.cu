@@ -351,6 +351,7 @@ int b200q_ep_pack(const void* x, int64_t T, int64_t D, int dtype, const int32_t*
   using namespace b200q;
   if (T < 0 || D <= 0 || D % 8 || P < 1 || E % P || E > moe::MAX_EXPERTS || C < 0 || P * C > (1ll << 30))
     return fail(B200Q_ERR_SHAPE, "ep_pack: need D % 8 == 0, E % P == 0, E <= 256");
+  if (C < 2 * T) return fail(B200Q_ERR_SHAPE, "ep_pack: need C >= 2 T (every pair may go to one rank)");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send)) & 15)
     return fail(B200Q_ERR_ALIGN, "ep_pack: x and send must be 16-byte aligned");
   if (P * C == 0) return B200Q_OK;
