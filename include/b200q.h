@@ -114,7 +114,8 @@ int b200q_silu_mul(const void* gate, const void* up, void* h, int64_t n, int dty
 
 /* y[t] = ye[token_slot[t,0]] * gates[t,0] + ye[token_slot[t,1]] * gates[t,1],
  * products and sum rounded to dtype as the reference's (sel * topv).sum(1)
- * (generate_tasks.py:377-378).  ye [2T, D], y [T, D]. */
+ * (generate_tasks.py:377-378).  ye [2T, D], y [T, D], D % 8 == 0, 16-byte
+ * aligned ye and y. */
 int b200q_moe_combine(const void* ye, const int32_t* token_slot, const void* gates, void* y, int64_t T, int64_t D,
                       int dtype, void* stream);
 
